@@ -1,0 +1,383 @@
+#!/usr/bin/env python
+"""Decode throughput of the Qwen2.5 decode token loop on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One JSON line (rank 0). A "step" is one greedy decode token of every sequence
+in flight. Workload (Qwen2.5-7B architecture, random-init bf16 weights, 2048-slot
+synthetic N(0,1) bf16 KV prefill per sequence):
+  * N=1: batch 1 through the whole model on one GPU; one persistent stage-kernel
+    launch per token, replayed as a CUDA graph with the token kept on device.
+  * N>1: contiguous layer stages, one per GPU (plan_stages), N sequences in
+    flight as micro-batches, hidden rows hopped to the next GPU with NCCL
+    send/recv (multigpu.py). Per-GPU work per step is fixed: weak scaling.
+`value` is tokens/s of the whole job timed with CUDA events on the launching
+stream (max over ranks); `e2e` is the same metric through the public generate
+call with the token copied host->device and back every step. Weights (15 GB)
+and KV exceed L2 (126 MB), so no L2 flush is needed between steps.
+
+`--impl reference` times the reference's CPU path: the reference is JavaScript +
+WebGPU with no runtime on this machine, so its loops are timed through the C++
+restatement (oracle/ref_forward.cpp, reference loop order) on all host cores,
+on a bounded sample of layers scaled to a full token.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tokens/s (bf16) at 1/2/4/8 B200; % of HBM roofline per token"
+UNIT = "tokens/s"
+KV_LEN = 2048
+WEIGHT_STD = 0.02
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
+    p.add_argument("--steps", type=int, default=128)
+    p.add_argument("--warmup", type=int, default=8)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--model", default="qwen2.5-7b")
+    p.add_argument("--kv-len", type=int, default=KV_LEN)
+    p.add_argument("--micro", type=int, default=1, help="sequences per micro-batch (N>1)")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-layers", type=int, default=2, help="layers in the CPU baseline sample")
+    p.add_argument("--cpu-steps", type=int, default=3, help="tokens in the CPU baseline sample")
+    return p.parse_args()
+
+
+def measured_peaks() -> tuple[float, str]:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def traffic_from_profile() -> float | None:
+    """DRAM bytes per stage-kernel launch from the committed ncu summary, if any
+    (line `dram_bytes_per_token_7b: <bytes>`)."""
+    path = os.path.join(ROOT, "profiles", "stage_kernel_qwen7b_decode.md")
+    try:
+        for line in open(path):
+            if line.strip().startswith("dram_bytes_per_token_7b:"):
+                return float(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+# ---- clocks --------------------------------------------------------------------------
+class ClockSampler:
+    """Samples SM clock and throttle reasons of one GPU through NVML while active."""
+
+    def __init__(self, index: int, period_s: float = 0.02):
+        self.index, self.period, self.samples, self.reasons = index, period_s, [], set()
+        self._stop = threading.Event()
+        self._t = None
+        self.max_mhz = None
+        self.ok = False
+
+    def __enter__(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            self.nv = nv
+            self.h = nv.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM)
+            self.ok = True
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        except Exception:
+            self.ok = False
+        return self
+
+    def _run(self):
+        nv = self.nv
+        names = {
+            "sw_power_cap": getattr(nv, "nvmlClocksEventReasonSwPowerCap", 0x4),
+            "hw_slowdown": getattr(nv, "nvmlClocksEventReasonHwSlowdown", 0x8),
+            "sw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+            "hw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+            "hw_power_brake_slowdown": getattr(nv, "nvmlClocksEventReasonHwPowerBrakeSlowdown", 0x80),
+        }
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for k, bit in names.items():
+                    if r & bit:
+                        self.reasons.add(k)
+            except Exception:
+                pass
+            self._stop.wait(self.period)
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=1)
+
+    def summary(self) -> dict:
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ---- model setup on the device ------------------------------------------------------
+def device_weights(ctx, stage, cfg, start: int, end: int, embed: bool, head: bool, seed: int = 0):
+    """Synthetic bf16 weights generated on the device: N(0, 0.02), norms 1.0."""
+    D, QD, KD, I, V = (cfg.hidden_size, cfg.num_q_heads * cfg.head_dim, cfg.num_kv_heads * cfg.head_dim,
+                       cfg.intermediate_size, cfg.vocab_size)
+    sizes = {"input_layernorm.weight": D, "post_attention_layernorm.weight": D,
+             "self_attn.q_proj.weight": QD * D, "self_attn.k_proj.weight": KD * D,
+             "self_attn.v_proj.weight": KD * D, "self_attn.o_proj.weight": D * QD,
+             "self_attn.q_proj.bias": QD, "self_attn.k_proj.bias": KD, "self_attn.v_proj.bias": KD,
+             "mlp.gate_proj.weight": I * D, "mlp.up_proj.weight": I * D, "mlp.down_proj.weight": D * I}
+    k = 0
+    for L in range(start, end):
+        for suf, n in sizes.items():
+            name = f"model.layers.{L}.{suf}"
+            b = ctx.createBf16(n, name)
+            if "layernorm" in suf:
+                ctx.fillConstBf16(b, 1.0)
+            else:
+                ctx.fillNormalBf16(b, seed * 100003 + L * 97 + k, WEIGHT_STD)
+            k += 1
+            stage.W[name] = b
+    bufs = {}
+    if embed or (head and cfg.tie_word_embeddings):
+        bufs["embed"] = ctx.createBf16(V * D, "model.embed_tokens.weight")
+        ctx.fillNormalBf16(bufs["embed"], seed * 100003 + 90001, WEIGHT_STD)
+        stage.W["model.embed_tokens.weight"] = bufs["embed"]
+    if head:
+        bufs["norm"] = ctx.createBf16(D, "model.norm.weight")
+        ctx.fillConstBf16(bufs["norm"], 1.0)
+        stage.W["model.norm.weight"] = bufs["norm"]
+        if not cfg.tie_word_embeddings:
+            bufs["lm_head"] = ctx.createBf16(V * D, "lm_head.weight")
+            ctx.fillNormalBf16(bufs["lm_head"], seed * 100003 + 90002, WEIGHT_STD)
+            stage.W["lm_head.weight"] = bufs["lm_head"]
+    return bufs
+
+
+def token_bytes(cfg, layers: int, head: bool, embed: bool, kv_positions: float) -> float:
+    """Algorithmic HBM bytes of one token through `layers` layers: bf16 weights
+    read once, plus K and V of every attended slot, plus the embedding row."""
+    b = layers * cfg.layer_weight_bytes()
+    if head:
+        b += cfg.head_weight_bytes()
+    if embed:
+        b += 2 * cfg.hidden_size
+    es = 2 if cfg.kv_dtype == "bf16" else 4
+    b += layers * 2 * cfg.num_kv_heads * cfg.head_dim * es * kv_positions
+    return b
+
+
+# ---- CPU baseline (oracle C++ restatement) ----------------------------------------------
+def _cpu_model(cfg, layers: int, kv_len: int, max_steps: int):
+    """The oracle's C++ restatement with synthetic weights for `layers` layers +
+    final norm + LM head, KV prefilled with `kv_len` slots."""
+    import ctypes as C
+    import subprocess
+
+    import numpy as np
+    so = os.path.join(ROOT, "oracle", "_build", "libref_forward.so")
+    if not os.path.exists(so):
+        subprocess.run(["make", "-C", os.path.join(ROOT, "oracle")], check=True, capture_output=True)
+    lib = C.CDLL(so)
+    cores = os.cpu_count() or 1
+    lib.ref_set_threads.argtypes = [C.c_int]
+    lib.ref_set_threads(cores)
+    lib.ref_fill_normal_bf16.argtypes = [C.c_void_p, C.c_size_t, C.c_uint64, C.c_float]
+    lib.ref_model_create.restype = C.c_void_p
+    lib.ref_model_create.argtypes = [C.c_void_p, C.c_float, C.c_float, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
+    lib.ref_stage_forward.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int]
+    lib.ref_sample_last.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p]
+    lib.ref_model_fill_kv.argtypes = [C.c_void_p, C.c_int, C.c_uint64]
+    lib.ref_model_destroy.argtypes = [C.c_void_p]
+    D, QD, KD, I, V = (cfg.hidden_size, cfg.num_q_heads * cfg.head_dim, cfg.num_kv_heads * cfg.head_dim,
+                       cfg.intermediate_size, cfg.vocab_size)
+    sizes = [D, D, QD * D, KD * D, KD * D, D * QD, QD, KD, KD, I * D, I * D, D * I]
+    keep, ptrs = [], (C.c_void_p * (12 * layers))()
+    for L in range(layers):
+        for i, n in enumerate(sizes):
+            a = np.empty(n, np.uint16)
+            if i < 2:
+                a[:] = 0x3F80  # norms = 1.0
+            else:
+                lib.ref_fill_normal_bf16(a.ctypes.data, n, 1000 + L * 12 + i, WEIGHT_STD)
+            keep.append(a)
+            ptrs[L * 12 + i] = a.ctypes.data
+    norm = np.full(D, 0x3F80, np.uint16)
+    head = np.empty(V * D, np.uint16)
+    lib.ref_fill_normal_bf16(head.ctypes.data, head.size, 77, WEIGHT_STD)
+    keep += [ptrs, norm, head]
+    kv_bf16 = 1 if getattr(cfg, "kv_dtype", "bf16") == "bf16" else 0
+    dims = (C.c_int * 10)(D, cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim, I, V, 0, layers,
+                          kv_len + max_steps + 2, kv_bf16)
+    keep.append(dims)
+    m = lib.ref_model_create(dims, cfg.rms_norm_eps, cfg.rope_theta, ptrs, head.ctypes.data, norm.ctypes.data,
+                             head.ctypes.data)
+    lib.ref_model_fill_kv(m, kv_len, 5)
+    return lib, m, keep, cores
+
+
+def cpu_token_times(cfg, layers: int, warmup: int, steps: int, kv_len: int):
+    """Per-token seconds of the reference loops for a full model, measured on a
+    sample of `layers` layers (scaled by num_layers / layers) plus the LM head."""
+    import numpy as np
+    lib, m, keep, cores = _cpu_model(cfg, layers, kv_len, warmup + steps)
+    h = np.random.default_rng(0).standard_normal(cfg.hidden_size).astype(np.float32) * np.float32(0.05)
+    times = []
+    for s in range(warmup + steps):
+        x = h.copy()
+        t0 = time.perf_counter()
+        lib.ref_stage_forward(m, x.ctypes.data, 1, kv_len + s)
+        t1 = time.perf_counter()
+        lib.ref_sample_last(m, x.ctypes.data, None)
+        t2 = time.perf_counter()
+        if s >= warmup:
+            times.append((t1 - t0) * (cfg.num_layers / layers) + (t2 - t1))
+    lib.ref_model_destroy(m)
+    return times, cores
+
+
+def cpu_baseline(cfg, layers: int, steps: int, kv_len: int) -> dict:
+    times, cores = cpu_token_times(cfg, layers, 1, steps, kv_len)
+    per_token = sum(times) / len(times)
+    return {"value": 1.0 / per_token, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": (f"{steps} decode tokens (+1 warm-up) through {layers} of {cfg.num_layers} layers + final "
+                       f"norm + LM head at {kv_len}-slot KV on {cores} host threads, layer time scaled "
+                       f"x{cfg.num_layers / layers:g}; oracle/ref_forward.cpp (reference loop order, fp32)")}
+
+
+def run_reference(args):
+    """The reference's CPU path through its C++ restatement (no package code)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import dataclasses
+
+    import synth
+    key = {"qwen2.5-0.5b": "0.5b", "qwen2.5-1.5b": "1.5b", "qwen2.5-7b": "7b", "qwen2.5-32b": "32b"}[args.model]
+    cfg = synth.CONFIGS[key]
+    cfg.kv_dtype = "bf16"
+    times, cores = cpu_token_times(cfg, args.cpu_layers, args.warmup, args.steps, args.kv_len)
+    v = len(times) / sum(times)
+    res = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "config": workload_config(args, cfg),
+           "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
+                            "sample": (f"each step: one decode token through {args.cpu_layers} of {cfg.num_layers} "
+                                       f"layers + final norm + LM head at {args.kv_len}-slot KV, layer time scaled "
+                                       f"x{cfg.num_layers / args.cpu_layers:g}; oracle/ref_forward.cpp")},
+           "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+           "note": "the reference is JavaScript + WebGPU with no JS engine or WebGPU adapter on this machine; "
+                   "its loops are timed through the C++ restatement"}
+    return res
+
+
+def workload_config(args, cfg) -> dict:
+    return {"workload": f"{args.model} greedy decode, {args.kv_len}-slot synthetic bf16 KV per sequence, "
+                        f"{'batch 1 on one GPU' if args.gpus == 1 else f'{args.gpus}-stage pipeline, {args.gpus} micro-batches of {args.micro}'}",
+            "batch": 1 if args.gpus == 1 else args.gpus * args.micro, "kv_len": args.kv_len,
+            "parallelism": f"pp{args.gpus}", "kv_dtype": getattr(cfg, "kv_dtype", "bf16"), "weights": "bf16",
+            "l2_policy": "inputs larger than L2 (weights 15 GB per token)"}
+
+
+# ---- our arm, one GPU ---------------------------------------------------------------------
+def run_single(args):
+    import torch
+    dllm = importlib.import_module("distributed-llm1_b200")
+    cfg = dllm.PRESETS[args.model].with_(kv_dtype="bf16",
+                                         max_pos=args.kv_len + 2 * (args.warmup + args.steps) + 64)
+    torch.cuda.set_device(0)
+    stream = torch.cuda.Stream()
+    ctx = dllm.initKernels(0, cfg)
+    ctx.set_stream(stream.cuda_stream)
+    ld = dllm.LeaderPipeline(ctx, (0, cfg.num_layers))
+    bufs = device_weights(ctx, ld.stage, cfg, 0, cfg.num_layers, embed=True, head=True)
+    ld.stage.fill_kv_random(0, args.kv_len, seed=1)
+    ctx.synchronize(120000)
+    first = 1234
+    # warmup (graph capture happens on the first call)
+    ld.decode_enqueue(first, args.warmup)
+    toks = ld.read_tokens(args.warmup)
+    t_start = ld.stage.T0
+    launches0 = ctx.launch_count
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        ld.decode_enqueue(toks[-1], args.steps)
+        ev1.record(stream)
+        ev1.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    out = ld.read_tokens(args.steps)
+    launches = ctx.launch_count - launches0
+    tps = args.steps / (ms / 1000.0)
+    avg_pos = t_start + (args.steps - 1) / 2.0 + 1
+    bytes_tok = token_bytes(cfg, cfg.num_layers, head=True, embed=True, kv_positions=avg_pos)
+    peak, peak_kind = measured_peaks()
+    achieved = bytes_tok / (ms / 1000.0 / args.steps) / 1e9
+    traffic = traffic_from_profile()
+    # e2e: public generate call, token in from / out to host every step
+    e2e_steps = args.steps
+    gen_out = []
+    ld.onToken = gen_out.append
+    ld.generate([out[-1]], 2)  # warm the e2e graph
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    ld.generate([out[-1]], e2e_steps)
+    e2e_s = time.perf_counter() - t0
+    e2e_tps = len(gen_out[2:]) / e2e_s if len(gen_out) > 2 else None
+    res = {"metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "bf16", "data": "synthetic: random-init N(0,0.02) bf16 weights (device hash), N(0,1) bf16 KV",
+           "config": workload_config(args, cfg),
+           "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                        "traffic": traffic, "peak_kind": peak_kind, "algorithmic_bytes_per_launch": bytes_tok,
+                        "kernel": "stage_kernel (one persistent launch per token)"},
+           "e2e": {"value": e2e_tps, "unit": UNIT, "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
+                   "api": "LeaderPipeline.generate -> dllm_leader_generate"},
+           "gpu_launches": launches, "clocks": clk.summary()}
+    if not args.no_cpu_baseline:
+        try:
+            res["cpu_baseline"] = cpu_baseline(cfg, args.cpu_layers, args.cpu_steps, args.kv_len)
+        except Exception as e:  # reported, never silently replaced
+            res["cpu_baseline"] = {"value": None, "error": repr(e)}
+    del bufs
+    ld.close()
+    ctx.close()
+    return res
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        res = run_reference(args)
+    elif args.gpus <= 1:
+        res = run_single(args)
+    else:
+        from importlib import import_module
+        mg = import_module("distributed-llm1_b200.multigpu")
+        res = mg.bench_pipeline(args, sys.modules[__name__])
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

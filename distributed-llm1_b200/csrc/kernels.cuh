@@ -1,0 +1,710 @@
+// kernels.cuh — device code of the decode path (sm_100a).
+//
+// The decode step of a pipeline stage runs as ONE persistent kernel
+// (stage_kernel in stage.cu): one CTA per SM, all CTAs co-resident (cooperative
+// launch), phases separated by a bounded grid barrier. Per decoder layer the
+// phases are
+//   QKV   : RMSNorm prologue + fused q|k|v matvec + bias + RoPE + KV-slot write
+//   ATTN  : split-K GQA decode attention over the paged KV cache + merge
+//   O     : o_proj matvec + residual add
+//   GATEUP: RMSNorm prologue + gate|up matvec + SiLU(gate)*up
+//   DOWN  : down_proj matvec + residual add
+// which is the op order of Stage.forward (pipeline.js:52-75). Optional first
+// and last phases gather the token embedding (pipeline.js:121-128) and run the
+// final norm + LM head + greedy argmax (pipeline.js:141-174).
+//
+// Every matvec phase streams bf16 weights with 16-byte loads, accumulates in
+// fp32, splits each row into K-segments spread over the CTA's 16 warps, and
+// reduces the segment partials in shared memory in a fixed order, so results do
+// not depend on scheduling. Work is split between CTAs by contiguous, equal
+// unit ranges (a unit is one row, or the row pair an epilogue needs together).
+// Before arriving at a barrier each CTA asks the TMA unit to prefetch the
+// weights of its next phase into L2, so HBM keeps streaming through the barrier.
+#pragma once
+
+#include "common.cuh"
+
+namespace dllm {
+
+constexpr int kThreads = 512;            // 16 warps per CTA, one CTA per SM
+constexpr int kWarps = kThreads / 32;
+constexpr int kU = 8;                    // 16-byte chunks per lane per task
+constexpr int kSegChunks = 32 * kU;      // 16-byte chunks per task segment (2048 bf16)
+constexpr int kSegElems = kSegChunks * 8;
+constexpr int kGMax = 8;                 // max query heads per KV head
+constexpr int kMaxRows = 8;              // max rows (sequences or prompt tokens) per pass
+
+// ---- block helpers ---------------------------------------------------------------
+DLLM_DEV float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int w = 0; w < nw; ++w) t += red[w];  // same fixed order in every thread
+  return t;
+}
+
+DLLM_DEV unsigned int ld_acquire_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Grid-wide barrier for a cooperative (all-CTAs-resident) launch. Sense is kept
+// by a monotonically increasing epoch, so no reset between launches is needed.
+// The wait is bounded: after ~2^33 SM cycles (seconds) the CTA records an error
+// and the caller leaves the kernel; the host reads the flag. Returns false on
+// timeout.
+constexpr long long kBarrierTimeoutCycles = 1ll << 33;
+constexpr int kErrBarrier = 2;
+constexpr int kErrKvRange = 3;
+constexpr int kErrToken = 4;
+
+DLLM_DEV bool grid_barrier(unsigned int* count, unsigned int* epoch, int* err) {
+  __syncthreads();
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    const unsigned int e = ld_acquire_u32(epoch);
+    __threadfence();
+    const unsigned int t = atomicAdd(count, 1u);
+    int ok = 1;
+    if (t == gridDim.x - 1) {
+      atomicExch(count, 0u);
+      __threadfence();
+      atomicAdd(epoch, 1u);
+    } else {
+      const long long t0 = clock64();
+      while (ld_acquire_u32(epoch) == e) {
+        if (clock64() - t0 > kBarrierTimeoutCycles) {
+          atomicExch(err, kErrBarrier);
+          ok = 0;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    __threadfence();
+    s_ok = ok;
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+
+// ---- activation staging (RMSNorm prologue, kernels.js:46-63) -----------------------
+// Per row: ss = sum(x^2), scale = 1 / sqrt(ss / K + eps), x' = (x * scale) * g.
+struct GemvIn {
+  const float* x;               // [m_rows][K], written earlier in the same kernel: L2 reads
+  int K;
+  int m_rows;                   // valid rows (<= M)
+  const __nv_bfloat16* norm_w;  // RMSNorm gamma [K] or null
+  float eps;
+};
+
+template <int M>
+DLLM_DEV void row_scales(const GemvIn& in, float* red, float (&scale)[M]) {
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+    scale[m] = 1.f;
+    if (!in.norm_w || m >= in.m_rows) continue;
+    const float4* src = reinterpret_cast<const float4*>(in.x + (size_t)m * in.K);
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < (in.K >> 2); i += blockDim.x) {
+      const float4 v = __ldcg(src + i);
+      ss = fmaf(v.x, v.x, ss);
+      ss = fmaf(v.y, v.y, ss);
+      ss = fmaf(v.z, v.z, ss);
+      ss = fmaf(v.w, v.w, ss);
+    }
+    const float tot = block_sum(ss, red);
+    scale[m] = 1.0f / sqrtf(tot / (float)in.K + in.eps);
+  }
+}
+
+// Stage columns [k0, k1) of every row into xs[m * xstride + (k - k0)].
+template <int M>
+DLLM_DEV void stage_x_block(const GemvIn& in, const float (&scale)[M], float* xs, int xstride, int k0, int k1) {
+  const int w4 = (k1 - k0) >> 2;
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+    float4* dst = reinterpret_cast<float4*>(xs + (size_t)m * xstride);
+    if (m >= in.m_rows) {
+      for (int i = threadIdx.x; i < w4; i += blockDim.x) dst[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      continue;
+    }
+    const float4* src = reinterpret_cast<const float4*>(in.x + (size_t)m * in.K + k0);
+    const uint2* g = in.norm_w ? reinterpret_cast<const uint2*>(in.norm_w + k0) : nullptr;
+    for (int i = threadIdx.x; i < w4; i += blockDim.x) {
+      float4 v = __ldcg(src + i);
+      if (g) {
+        const uint2 gg = __ldg(g + i);
+        v.x = (v.x * scale[m]) * bf16_lo(gg.x);
+        v.y = (v.y * scale[m]) * bf16_hi(gg.x);
+        v.z = (v.z * scale[m]) * bf16_lo(gg.y);
+        v.w = (v.w * scale[m]) * bf16_hi(gg.y);
+      }
+      dst[i] = v;
+    }
+  }
+  __syncthreads();
+}
+
+// Shared-memory budget a phase may use (floats).
+struct PhaseSmem {
+  float* xs;
+  int xs_floats;
+  float* part;
+  int part_floats;
+  float* red;  // >= 32 floats
+};
+
+// ---- matvec phase ----------------------------------------------------------------
+// Epi supplies: R (rows per unit), unit_rows(u, K, p[R]) and unit(u, m, a[R], st).
+// CTA `cta` of `ncta` owns units [cta*units/ncta, (cta+1)*units/ncta).
+template <class Epi, int M>
+DLLM_DEV void gemv_phase(const Epi& epi, const GemvIn& in, int units, const PhaseSmem& sm, int cta, int ncta,
+                         typename Epi::State& st) {
+  constexpr int R = Epi::R;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int K = in.K, Kc = K >> 3;
+  const int u0 = (int)(((long long)cta * units) / ncta);
+  const int u1 = (int)(((long long)(cta + 1) * units) / ncta);
+  const int nu = u1 - u0;
+  const int nseg = (Kc + kSegChunks - 1) / kSegChunks;
+  int seg_per_blk = sm.xs_floats / (M * kSegElems);
+  if (seg_per_blk < 1) seg_per_blk = 1;
+  if (seg_per_blk > nseg) seg_per_blk = nseg;
+  const int nblk = (nseg + seg_per_blk - 1) / seg_per_blk;
+  const int xstride = seg_per_blk * kSegElems;
+  int ub = sm.part_floats / (nseg * R * M);
+  if (ub < 1) ub = 1;
+
+  float scale[M];
+  row_scales<M>(in, sm.red, scale);
+  if (nu <= 0) return;
+
+  for (int b0 = 0; b0 < nu; b0 += ub) {
+    const int nb = min(ub, nu - b0);
+    for (int blk = 0; blk < nblk; ++blk) {
+      const int s0 = blk * seg_per_blk, s1 = min(nseg, s0 + seg_per_blk);
+      const int k0 = s0 * kSegElems, k1 = min(K, s1 * kSegElems);
+      if (nblk > 1 || b0 == 0) {
+        __syncthreads();  // previous readers of xs are done
+        stage_x_block<M>(in, scale, sm.xs, xstride, k0, k1);
+      }
+      const int nsb = s1 - s0;
+      const int ntask = nb * nsb;
+      for (int t = warp; t < ntask; t += nwarps) {
+        const int ul = t / nsb, seg = s0 + (t - ul * nsb);
+        const uint4* p[R];
+        epi.unit_rows(u0 + b0 + ul, K, p);
+        const int cbase = seg * kSegChunks + lane;
+        uint4 w[kU][R];
+#pragma unroll
+        for (int i = 0; i < kU; ++i) {
+          const int ci = cbase + 32 * i;
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            if (ci < Kc) w[i][r] = ld_stream16(p[r] + ci);
+            else w[i][r] = make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+        float acc[R][M];
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+          for (int m = 0; m < M; ++m) acc[r][m] = 0.f;
+#pragma unroll
+        for (int i = 0; i < kU; ++i) {
+          const int ci = cbase + 32 * i;
+          if (ci < Kc) {
+            const int xo = ci * 8 - k0;
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+              const float4* xr = reinterpret_cast<const float4*>(sm.xs + (size_t)m * xstride + xo);
+              const float4 a = xr[0], b = xr[1];
+#pragma unroll
+              for (int r = 0; r < R; ++r) acc[r][m] = dot8(w[i][r], a, b, acc[r][m]);
+            }
+          }
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+          for (int m = 0; m < M; ++m) acc[r][m] = warp_sum(acc[r][m]);
+        if (lane == 0) {
+          float* dst = sm.part + ((size_t)ul * nseg + seg) * (R * M);
+#pragma unroll
+          for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int m = 0; m < M; ++m) dst[r * M + m] = acc[r][m];
+        }
+      }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < nb * M; i += blockDim.x) {
+      const int ul = i / M, m = i - ul * M;
+      if (m >= in.m_rows) continue;
+      float a[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        float s = 0.f;
+        for (int seg = 0; seg < nseg; ++seg) s += sm.part[((size_t)ul * nseg + seg) * (R * M) + r * M + m];
+        a[r] = s;
+      }
+      epi.unit(u0 + b0 + ul, m, a, st);
+    }
+    __syncthreads();
+  }
+}
+
+// Ask the TMA unit to pull up to `budget` bytes of this CTA's rows of a future
+// matvec phase into L2 (whole rows, in unit order). Issued by warp 0.
+template <class Epi>
+DLLM_DEV void prefetch_phase(const Epi& epi, int K, int units, int cta, int ncta, int budget) {
+  if (budget <= 0 || (threadIdx.x >> 5) != 0) return;
+  const int lane = threadIdx.x & 31;
+  const int u0 = (int)(((long long)cta * units) / ncta);
+  const int u1 = (int)(((long long)(cta + 1) * units) / ncta);
+  const int row_bytes = K * 2;
+  const int max_units = budget / (row_bytes * Epi::R);
+  const int uend = min(u1, u0 + max(1, max_units));
+  for (int u = u0 + lane; u < uend; u += 32) {
+    const uint4* p[Epi::R];
+    epi.unit_rows(u, K, p);
+#pragma unroll
+    for (int r = 0; r < Epi::R; ++r) prefetch_l2_bulk(p[r], (uint32_t)row_bytes);
+  }
+}
+
+// ---- epilogues ---------------------------------------------------------------------
+struct NoState {};
+
+// out[m][j] = x[m] . W[j]  (ctx.matmul, kernels.js:26-44)
+struct EpiStore {
+  static constexpr int R = 1;
+  using State = NoState;
+  const __nv_bfloat16* w;
+  float* y;
+  int N;
+  DLLM_DEV void unit_rows(int u, int K, const uint4** p) const {
+    p[0] = reinterpret_cast<const uint4*>(w + (size_t)u * K);
+  }
+  DLLM_DEV void unit(int u, int m, const float* a, State&) const { y[(size_t)m * N + u] = a[0]; }
+};
+
+// h[m][j] = h[m][j] + x[m] . W[j]  (o_proj / down_proj then ctx.add, pipeline.js:66-67,73-74)
+struct EpiResidual {
+  static constexpr int R = 1;
+  using State = NoState;
+  const __nv_bfloat16* w;
+  float* h;
+  int N;
+  DLLM_DEV void unit_rows(int u, int K, const uint4** p) const {
+    p[0] = reinterpret_cast<const uint4*>(w + (size_t)u * K);
+  }
+  DLLM_DEV void unit(int u, int m, const float* a, State&) const {
+    float* d = h + (size_t)m * N + u;
+    *d = __fadd_rn(__ldcg(d), a[0]);
+  }
+};
+
+// mid[m][j] = silu(x.Wg[j]) * (x.Wu[j])  (gate/up matmuls + ctx.siluMul, pipeline.js:70-72;
+// SILUMUL kernels.js:134-145: a / (1 + exp(-a)) * b)
+struct EpiSiluGate {
+  static constexpr int R = 2;
+  using State = NoState;
+  const __nv_bfloat16* wg;
+  const __nv_bfloat16* wu;
+  float* out;
+  int N;
+  DLLM_DEV void unit_rows(int u, int K, const uint4** p) const {
+    p[0] = reinterpret_cast<const uint4*>(wg + (size_t)u * K);
+    p[1] = reinterpret_cast<const uint4*>(wu + (size_t)u * K);
+  }
+  DLLM_DEV void unit(int u, int m, const float* a, State&) const {
+    const float g = a[0];
+    const float silu = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+    out[(size_t)m * N + u] = __fmul_rn(silu, a[1]);
+  }
+};
+
+// q|k|v projection of one rotate-half pair (rows j and j + HD/2 of one head),
+// + bias (ctx.addBias, kernels.js:148-159), + RoPE for q and k (ROPE,
+// kernels.js:66-83), then q -> q buffer and k, v -> KV slot `slot` of the row's
+// sequence (Stage.appendKv, pipeline.js:80-87).
+template <typename KT>
+struct EpiQKV {
+  static constexpr int R = 2;
+  using State = NoState;
+  const __nv_bfloat16 *wq, *wk, *wv;
+  const __nv_bfloat16 *bq, *bk, *bv;
+  int NQ, KVH, HD, log2_half;
+  const float* freq;  // [HD/2] RoPE inverse frequencies (f32)
+  float* q_out;       // [m][NQ*HD]
+  KT* kc;             // this layer's K pool
+  KT* vc;             // this layer's V pool
+  KvLayout kv;
+  const RowDesc* rows;
+  int* err;
+
+  DLLM_DEV void locate(int u, int& kind, int& lh, int& half) const {
+    const int hh = u >> log2_half;
+    half = u & ((1 << log2_half) - 1);
+    if (hh < NQ) {
+      kind = 0;
+      lh = hh;
+    } else if (hh < NQ + KVH) {
+      kind = 1;
+      lh = hh - NQ;
+    } else {
+      kind = 2;
+      lh = hh - NQ - KVH;
+    }
+  }
+  DLLM_DEV void unit_rows(int u, int K, const uint4** p) const {
+    int kind, lh, half;
+    locate(u, kind, lh, half);
+    const __nv_bfloat16* w = kind == 0 ? wq : (kind == 1 ? wk : wv);
+    const size_t r0 = (size_t)lh * HD + half;
+    p[0] = reinterpret_cast<const uint4*>(w + r0 * K);
+    p[1] = reinterpret_cast<const uint4*>(w + (r0 + (HD >> 1)) * K);
+  }
+  DLLM_DEV void unit(int u, int m, const float* a, State&) const {
+    int kind, lh, half;
+    locate(u, kind, lh, half);
+    const int j0 = lh * HD + half, j1 = j0 + (HD >> 1);
+    float x1 = a[0], x2 = a[1];
+    const __nv_bfloat16* b = kind == 0 ? bq : (kind == 1 ? bk : bv);
+    if (b) {
+      x1 = __fadd_rn(x1, bf16_to_f32(b[j0]));
+      x2 = __fadd_rn(x2, bf16_to_f32(b[j1]));
+    }
+    const RowDesc rd = rows[m];
+    if (kind < 2) {
+      const float ang = __fmul_rn((float)rd.pos, freq[half]);
+      float s, c;
+      sincosf(ang, &s, &c);
+      const float o1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+      const float o2 = __fadd_rn(__fmul_rn(x1, s), __fmul_rn(x2, c));
+      x1 = o1;
+      x2 = o2;
+    }
+    if (kind == 0) {
+      float* q = q_out + (size_t)m * NQ * HD;
+      q[j0] = x1;
+      q[j1] = x2;
+      return;
+    }
+    if (rd.slot < 0 || rd.slot >= kv.max_slots || rd.seq < 0 || rd.seq >= kv.num_seqs) {
+      atomicExch(err, kErrKvRange);
+      return;
+    }
+    KT* base = (kind == 1 ? kc : vc) + kv.offset(rd.seq, rd.slot, lh);
+    store_kv(base + half, x1);
+    store_kv(base + half + (HD >> 1), x2);
+  }
+  DLLM_DEV static void store_kv(float* p, float v) { *p = v; }
+  DLLM_DEV static void store_kv(__nv_bfloat16* p, float v) { *p = f32_to_bf16(v); }
+};
+
+// Final norm + LM head + greedy argmax (sampleLast, pipeline.js:141-174). Each
+// thread keeps the best (value, index) key per row; the CTA folds them with
+// atomicMax into best[m]. Optionally writes the logits.
+template <int M>
+struct EpiArgmax {
+  static constexpr int R = 1;
+  struct State {
+    unsigned long long key[M];
+  };
+  const __nv_bfloat16* w;
+  int N;
+  float* logits;  // [m][N] or null
+  DLLM_DEV void unit_rows(int u, int K, const uint4** p) const {
+    p[0] = reinterpret_cast<const uint4*>(w + (size_t)u * K);
+  }
+  DLLM_DEV void unit(int u, int m, const float* a, State& st) const {
+    if (logits) logits[(size_t)m * N + u] = a[0];
+    const unsigned long long k = argmax_key(a[0], u);
+#pragma unroll
+    for (int i = 0; i < M; ++i)
+      if (i == m && k > st.key[i]) st.key[i] = k;
+  }
+};
+
+// ---- decode attention phase (ATTENTION, kernels.js:86-132) ------------------------------
+// Row m's query attends to slots [0, slot_m] of its sequence. Work item =
+// (row, kv head g, split s): a split is a contiguous range of slots; the CTA's
+// warps take 32-slot sub-chunks. For the G query heads sharing kv head g
+// (h / (NQ/KVH) == g, kernels.js:97) a lane owns one slot for q.k (no
+// shuffles), then owns HD/32 dims for p.V. Online softmax per warp, combined
+// across warps in shared memory and across splits by the last CTA to finish the
+// (row, g) pair (atomic ticket, no waiting).
+struct AttnArgs {
+  const float* q;     // [M][NQ*HD]
+  float* out;         // [M][NQ*HD]
+  const void* kc;     // this layer's K pool
+  const void* vc;
+  KvLayout kv;
+  const RowDesc* rows;
+  int m_rows, NQ, KVH;
+  float scale;        // f32(1/sqrt(HD)), applied after the dot (kernels.js:106)
+  int max_splits;     // per (row, kv head)
+  float* part_o;      // [M][NQ][max_splits][HD]
+  float* part_ml;     // [M][NQ][max_splits][2]
+  unsigned int* arrive;  // [M][KVH], zero between uses
+  int* err;
+};
+
+DLLM_DEV int attn_splits(int T, int max_splits, int* chunk_out) {
+  int ns = (T + 31) / 32;
+  if (ns > max_splits) ns = max_splits;
+  if (ns < 1) ns = 1;
+  int chunk = (T + ns - 1) / ns;
+  chunk = (chunk + 31) & ~31;
+  ns = (T + chunk - 1) / chunk;
+  *chunk_out = chunk;
+  return ns;
+}
+
+// 16-byte KV vector: 4 fp32 or 8 bf16 elements (slot row of the q.k pass).
+template <typename KT>
+struct KvVec16;
+template <>
+struct KvVec16<float> {
+  static constexpr int N = 4;
+  DLLM_DEV static void load(const float* p, float (&v)[4]) {
+    const float4 t = __ldcg(reinterpret_cast<const float4*>(p));
+    v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+  }
+};
+template <>
+struct KvVec16<__nv_bfloat16> {
+  static constexpr int N = 8;
+  DLLM_DEV static void load(const __nv_bfloat16* p, float (&v)[8]) {
+    const uint4 t = __ldcg(reinterpret_cast<const uint4*>(p));
+    v[0] = bf16_lo(t.x); v[1] = bf16_hi(t.x); v[2] = bf16_lo(t.y); v[3] = bf16_hi(t.y);
+    v[4] = bf16_lo(t.z); v[5] = bf16_hi(t.z); v[6] = bf16_lo(t.w); v[7] = bf16_hi(t.w);
+  }
+};
+
+template <typename KT>
+DLLM_DEV void load_vec4(const KT* p, float (&v)[4]);
+template <>
+DLLM_DEV void load_vec4<float>(const float* p, float (&v)[4]) {
+  const float4 t = __ldcg(reinterpret_cast<const float4*>(p));
+  v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+}
+template <>
+DLLM_DEV void load_vec4<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[4]) {
+  const uint2 t = __ldcg(reinterpret_cast<const uint2*>(p));
+  v[0] = bf16_lo(t.x); v[1] = bf16_hi(t.x); v[2] = bf16_lo(t.y); v[3] = bf16_hi(t.y);
+}
+template <typename KT>
+DLLM_DEV void load_vec2(const KT* p, float (&v)[2]);
+template <>
+DLLM_DEV void load_vec2<float>(const float* p, float (&v)[2]) {
+  const float2 t = __ldcg(reinterpret_cast<const float2*>(p));
+  v[0] = t.x; v[1] = t.y;
+}
+template <>
+DLLM_DEV void load_vec2<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[2]) {
+  const uint32_t t = __ldcg(reinterpret_cast<const unsigned int*>(p));
+  v[0] = bf16_lo(t); v[1] = bf16_hi(t);
+}
+
+// Attention for one work item; called by the whole CTA. smem needs
+// kGMax*HD (q) + kWarps*kGMax*32 (p) + kWarps*kGMax*(HD+2) (warp combine) floats.
+template <typename KT, int HD>
+DLLM_DEV void attn_item(const AttnArgs& A, int m, int g, int s, int nsplit, int chunk, float* smem) {
+  constexpr int DPL = HD / 32;  // dims per lane in p.V
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int G = A.NQ / A.KVH;
+  const RowDesc rd = A.rows[m];
+  const int T = rd.slot + 1;
+  const int p0 = s * chunk, p1 = min(T, p0 + chunk);
+  float* qs = smem;                          // [kGMax][HD]
+  float* ps = qs + kGMax * HD;               // [kWarps][kGMax][32]
+  float* wm = ps + kWarps * kGMax * 32;      // [kWarps][kGMax]
+  float* wl = wm + kWarps * kGMax;           // [kWarps][kGMax]
+  float* wacc = wl + kWarps * kGMax;         // [kWarps][kGMax][HD]
+
+  const float* qrow = A.q + (size_t)m * A.NQ * HD + (size_t)g * G * HD;
+  for (int i = threadIdx.x; i < G * HD; i += blockDim.x) qs[i] = __ldcg(qrow + i);
+  __syncthreads();
+
+  float mrun[kGMax], lsum[kGMax], acc[kGMax][DPL];
+#pragma unroll
+  for (int h = 0; h < kGMax; ++h) {
+    mrun[h] = -INFINITY;
+    lsum[h] = 0.f;
+#pragma unroll
+    for (int d = 0; d < DPL; ++d) acc[h][d] = 0.f;
+  }
+  const KT* kc = reinterpret_cast<const KT*>(A.kc);
+  const KT* vc = reinterpret_cast<const KT*>(A.vc);
+  float* myps = ps + warp * kGMax * 32;
+
+  for (int base = p0 + warp * 32; base < p1; base += nwarps * 32) {
+    // slots base..base+31 share one KV page (pages hold >= 32 slots, base % 32 == 0)
+    const long long off0 = A.kv.offset(rd.seq, base, g);
+    const int pos = base + lane;
+    const bool valid = pos < p1;
+    float sc[kGMax];
+#pragma unroll
+    for (int h = 0; h < kGMax; ++h) sc[h] = 0.f;
+    if (valid) {
+      constexpr int VE = KvVec16<KT>::N;
+      const KT* kr = kc + off0 + (long long)lane * A.kv.row_stride;
+#pragma unroll 4
+      for (int d = 0; d < HD; d += VE) {
+        float kv[VE];
+        KvVec16<KT>::load(kr + d, kv);
+#pragma unroll
+        for (int h = 0; h < kGMax; ++h) {
+          if (h < G) {
+            const float* qh = qs + h * HD + d;
+#pragma unroll
+            for (int e = 0; e < VE; ++e) sc[h] = fmaf(qh[e], kv[e], sc[h]);
+          }
+        }
+      }
+    }
+    float alpha[kGMax];
+#pragma unroll
+    for (int h = 0; h < kGMax; ++h) {
+      if (h < G) {
+        const float sv = valid ? __fmul_rn(sc[h], A.scale) : -INFINITY;
+        const float mx = warp_max(sv);
+        const float mnew = fmaxf(mrun[h], mx);
+        alpha[h] = (mrun[h] == -INFINITY) ? 0.f : expf(mrun[h] - mnew);
+        const float pv = valid ? expf(sv - mnew) : 0.f;
+        lsum[h] = fmaf(lsum[h], alpha[h], pv);
+        mrun[h] = mnew;
+        myps[h * 32 + lane] = pv;
+      }
+    }
+    __syncwarp();
+    const int npos = min(32, p1 - base);
+#pragma unroll
+    for (int h = 0; h < kGMax; ++h)
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) acc[h][d] *= (h < G) ? alpha[h] : 1.f;
+    const KT* vbase = vc + off0 + lane * DPL;
+#pragma unroll 4
+    for (int j = 0; j < npos; ++j) {
+      float vv[DPL];
+      if constexpr (DPL == 4) load_vec4<KT>(vbase + (long long)j * A.kv.row_stride, vv);
+      else load_vec2<KT>(vbase + (long long)j * A.kv.row_stride, vv);
+#pragma unroll
+      for (int h = 0; h < kGMax; ++h) {
+        if (h < G) {
+          const float pj = myps[h * 32 + j];
+#pragma unroll
+          for (int d = 0; d < DPL; ++d) acc[h][d] = fmaf(pj, vv[d], acc[h][d]);
+        }
+      }
+    }
+    __syncwarp();
+  }
+  // warp results -> smem
+#pragma unroll
+  for (int h = 0; h < kGMax; ++h) {
+    if (h < G) {
+      const float l = warp_sum(lsum[h]);
+      if (lane == 0) {
+        wm[warp * kGMax + h] = mrun[h];
+        wl[warp * kGMax + h] = l;
+      }
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) wacc[((size_t)warp * kGMax + h) * HD + lane * DPL + d] = acc[h][d];
+    }
+  }
+  __syncthreads();
+  // combine warps: thread per (h, d)
+  float* out_row = A.out + (size_t)m * A.NQ * HD + (size_t)g * G * HD;
+  for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
+    const int h = i / HD, d = i - h * HD;
+    float mx = -INFINITY;
+    for (int w = 0; w < nwarps; ++w) mx = fmaxf(mx, wm[w * kGMax + h]);
+    float l = 0.f, o = 0.f;
+    for (int w = 0; w < nwarps; ++w) {
+      const float mw = wm[w * kGMax + h];
+      if (mw == -INFINITY) continue;
+      const float f = expf(mw - mx);
+      l = fmaf(wl[w * kGMax + h], f, l);
+      o = fmaf(wacc[((size_t)w * kGMax + h) * HD + d], f, o);
+    }
+    if (nsplit == 1) {
+      out_row[h * HD + d] = __fdiv_rn(o, l);
+    } else {
+      const int hq = g * G + h;
+      A.part_o[(((size_t)m * A.NQ + hq) * A.max_splits + s) * HD + d] = o;
+      if (d == 0) {
+        float* ml = A.part_ml + (((size_t)m * A.NQ + hq) * A.max_splits + s) * 2;
+        ml[0] = mx;
+        ml[1] = l;
+      }
+    }
+  }
+  if (nsplit == 1) {
+    __syncthreads();
+    return;
+  }
+  // last CTA to finish this (row, g) merges the splits
+  __threadfence();
+  __syncthreads();
+  __shared__ int s_last;
+  if (threadIdx.x == 0) {
+    const unsigned int t = atomicAdd(&A.arrive[m * A.KVH + g], 1u);
+    s_last = (t == (unsigned int)nsplit - 1);
+  }
+  __syncthreads();
+  if (s_last) {
+    __threadfence();
+    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
+      const int h = i / HD, d = i - h * HD;
+      const int hq = g * G + h;
+      const float* ml = A.part_ml + ((size_t)m * A.NQ + hq) * A.max_splits * 2;
+      const float* po = A.part_o + ((size_t)m * A.NQ + hq) * A.max_splits * HD;
+      float mx = -INFINITY;
+      for (int k = 0; k < nsplit; ++k) mx = fmaxf(mx, __ldcg(ml + 2 * k));
+      float l = 0.f, o = 0.f;
+      for (int k = 0; k < nsplit; ++k) {
+        const float f = expf(__ldcg(ml + 2 * k) - mx);
+        l = fmaf(__ldcg(ml + 2 * k + 1), f, l);
+        o = fmaf(__ldcg(po + (size_t)k * HD + d), f, o);
+      }
+      out_row[h * HD + d] = __fdiv_rn(o, l);
+    }
+    if (threadIdx.x == 0) A.arrive[m * A.KVH + g] = 0u;
+  }
+  __syncthreads();
+}
+
+// All attention work items of a pass, spread round-robin over the CTAs.
+template <typename KT, int HD>
+DLLM_DEV void attn_phase(const AttnArgs& A, float* smem, int cta, int ncta) {
+  // enumerate items: rows in order, kv heads, splits
+  int item = 0;
+  for (int m = 0; m < A.m_rows; ++m) {
+    const RowDesc rd = A.rows[m];
+    if (rd.slot < 0 || rd.slot >= A.kv.max_slots || rd.seq < 0 || rd.seq >= A.kv.num_seqs) {
+      if (cta == 0 && threadIdx.x == 0) atomicExch(A.err, kErrKvRange);
+      continue;
+    }
+    int chunk;
+    const int ns = attn_splits(rd.slot + 1, A.max_splits, &chunk);
+    const int n_items = A.KVH * ns;
+    // items [item, item + n_items) of this row
+    for (int j = 0; j < n_items; ++j) {
+      if ((item + j) % ncta != cta) continue;
+      const int g = j / ns, s = j - g * ns;
+      attn_item<KT, HD>(A, m, g, s, ns, chunk, smem);
+    }
+    item += n_items;
+  }
+}
+
+}  // namespace dllm

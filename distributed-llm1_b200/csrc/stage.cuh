@@ -1,0 +1,71 @@
+// stage.cuh — parameters of the persistent stage kernel and its host launcher.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace dllm {
+
+// Weights and KV pools of one decoder layer (HF tensor names, weights.js:167-182).
+struct LayerW {
+  const __nv_bfloat16 *ln1, *ln2;         // input_layernorm, post_attention_layernorm
+  const __nv_bfloat16 *wq, *wk, *wv, *wo; // self_attn.{q,k,v,o}_proj.weight [out, in]
+  const __nv_bfloat16 *bq, *bk, *bv;      // self_attn.{q,k,v}_proj.bias (may be null)
+  const __nv_bfloat16 *wg, *wu, *wd;      // mlp.{gate,up,down}_proj.weight
+  void* kc;                               // K pool of this layer
+  void* vc;                               // V pool of this layer
+};
+
+struct StageParams {
+  int D, NQ, KVH, HD, I, V, log2_half;
+  float eps, scale;
+  int n_layers;
+  const LayerW* layers;  // device array [n_layers]
+  const float* freq;     // [HD/2]
+  int m_rows;            // rows of this pass (<= template M)
+  RowDesc* rows;         // [m_rows]
+  float* h;              // [M][D] residual stream, in/out
+  float* q;              // [M][NQ*HD]
+  float* att;            // [M][NQ*HD]
+  float* mid;            // [M][I]
+  float* part_o;         // attention split partials
+  float* part_ml;
+  unsigned int* arrive;  // [M][KVH]
+  int max_splits;
+  KvLayout kv;           // k/v bases unused (per layer in LayerW)
+  // optional first phase: h[m] = embed[tokens_in[m]]
+  const int32_t* tokens_in;
+  const __nv_bfloat16* embed;
+  // optional last phase: final norm + LM head + argmax
+  const __nv_bfloat16* final_norm;
+  const __nv_bfloat16* lm_head;
+  unsigned long long* best;  // [M], zero between uses
+  int32_t* tokens_out;       // [M]
+  float* logits;             // [logits_cap][M][V] or null
+  int logits_cap;
+  int* step_count;           // steps completed (indexes logits/history), or null
+  int32_t* history;          // [hist_cap][M] or null
+  int hist_cap;
+  int advance_rows;          // pos++ and slot++ for every row at the end
+  unsigned int* bar_count;
+  unsigned int* bar_epoch;
+  int* err;
+  int pref_bytes;            // per-CTA L2 prefetch budget for the next phase
+  int xs_floats;             // dynamic smem partition
+  int part_floats;
+};
+
+// Dynamic shared memory the stage kernel is launched with.
+constexpr int kStageXsFloats = 32768;    // 128 KB of staged activations
+constexpr int kStagePartFloats = 16384;  // 64 KB of segment partials
+constexpr size_t kStageSmemBytes = (size_t)(kStageXsFloats + kStagePartFloats) * sizeof(float);
+
+// Launches stage_kernel<KT, HD, M> with M the smallest of {1,2,4,8} >= m_rows,
+// one CTA per SM, cooperative (all CTAs resident). kv_dtype: 0 fp32, 1 bf16.
+cudaError_t launch_stage(const StageParams& p, int kv_dtype, int grid, cudaStream_t st);
+// Raise the dynamic shared-memory limit of every stage kernel instantiation on
+// the current device (call once per device, before any launch or capture).
+cudaError_t configure_stage_kernels();
+
+}  // namespace dllm

@@ -1,0 +1,172 @@
+// stage_impl.cuh — the persistent decode-step kernel of one pipeline stage
+// (template; instantiated per KV dtype in stage_f32.cu and stage_bf16.cu).
+//
+// One launch runs [embed] -> layers [start, end) -> [final norm + LM head +
+// argmax] for up to 8 rows (sequences of a micro-batch, or prompt tokens of a
+// prefill chunk). CTAs are one per SM and co-resident (cooperative launch);
+// phases are separated by grid_barrier(). See kernels.cuh for the phases.
+#pragma once
+#include "kernels.cuh"
+#include "stage.cuh"
+
+namespace dllm {
+
+template <typename KT, int HD, int M>
+__global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P) {
+  extern __shared__ __align__(16) float smem[];
+  __shared__ float red[32];
+  __shared__ unsigned long long sbest[kMaxRows];
+  const int cta = blockIdx.x, ncta = gridDim.x;
+  const PhaseSmem sm{smem, P.xs_floats, smem + P.xs_floats, P.part_floats, red};
+  NoState ns;
+  const int D = P.D, QD = P.NQ * P.HD;
+  const int qkv_units = (P.NQ + 2 * P.KVH) * (P.HD >> 1);
+
+  // Weights never depend on earlier phases: warm L2 for the first matvec.
+  if (P.n_layers > 0) {
+    const LayerW L0 = P.layers[0];
+    EpiQKV<KT> e0{L0.wq, L0.wk, L0.wv, nullptr, nullptr, nullptr, P.NQ, P.KVH, P.HD, P.log2_half};
+    prefetch_phase(e0, D, qkv_units, cta, ncta, P.pref_bytes);
+  }
+
+  if (P.tokens_in) {
+    // embedTokens (pipeline.js:121-128): bf16 row -> fp32, 8 elements per thread.
+    const int chunks = D >> 3;
+    const int c0 = (int)(((long long)cta * chunks) / ncta), c1 = (int)(((long long)(cta + 1) * chunks) / ncta);
+    for (int m = 0; m < P.m_rows; ++m) {
+      int tok = P.tokens_in[m];
+      if (tok < 0 || tok >= P.V) {
+        if (threadIdx.x == 0) atomicExch(P.err, kErrToken);
+        tok = 0;
+      }
+      const uint4* src = reinterpret_cast<const uint4*>(P.embed + (size_t)tok * D);
+      for (int c = c0 + threadIdx.x; c < c1; c += blockDim.x) {
+        const uint4 w = __ldg(src + c);
+        float4* dst = reinterpret_cast<float4*>(P.h + (size_t)m * D) + 2 * c;
+        dst[0] = make_float4(bf16_lo(w.x), bf16_hi(w.x), bf16_lo(w.y), bf16_hi(w.y));
+        dst[1] = make_float4(bf16_lo(w.z), bf16_hi(w.z), bf16_lo(w.w), bf16_hi(w.w));
+      }
+    }
+    if (!grid_barrier(P.bar_count, P.bar_epoch, P.err)) return;
+  }
+
+  for (int l = 0; l < P.n_layers; ++l) {
+    const LayerW L = P.layers[l];
+    // ---- QKV: rmsnorm -> q,k,v matmul -> addBias -> ropeQ/ropeK -> appendKv (pipeline.js:55-64)
+    const EpiQKV<KT> eq{L.wq, L.wk, L.wv, L.bq, L.bk, L.bv, P.NQ, P.KVH, P.HD, P.log2_half, P.freq, P.q,
+                        reinterpret_cast<KT*>(L.kc), reinterpret_cast<KT*>(L.vc), P.kv, P.rows, P.err};
+    gemv_phase<EpiQKV<KT>, M>(eq, GemvIn{P.h, D, P.m_rows, L.ln1, P.eps}, qkv_units, sm, cta, ncta, ns);
+    const EpiResidual eo{L.wo, P.h, D};
+    prefetch_phase(eo, QD, D, cta, ncta, P.pref_bytes);
+    if (!grid_barrier(P.bar_count, P.bar_epoch, P.err)) return;
+
+    // ---- attention over slots [0, slot] (pipeline.js:65)
+    const AttnArgs A{P.q, P.att, L.kc, L.vc, P.kv, P.rows, P.m_rows, P.NQ, P.KVH, P.scale, P.max_splits,
+                     P.part_o, P.part_ml, P.arrive, P.err};
+    attn_phase<KT, HD>(A, smem, cta, ncta);
+    if (!grid_barrier(P.bar_count, P.bar_epoch, P.err)) return;
+
+    // ---- o_proj + residual (pipeline.js:66-67)
+    gemv_phase<EpiResidual, M>(eo, GemvIn{P.att, QD, P.m_rows, nullptr, 0.f}, D, sm, cta, ncta, ns);
+    const EpiSiluGate eg{L.wg, L.wu, P.mid, P.I};
+    prefetch_phase(eg, D, P.I, cta, ncta, P.pref_bytes);
+    if (!grid_barrier(P.bar_count, P.bar_epoch, P.err)) return;
+
+    // ---- rmsnorm -> gate, up -> siluMul (pipeline.js:69-72)
+    gemv_phase<EpiSiluGate, M>(eg, GemvIn{P.h, D, P.m_rows, L.ln2, P.eps}, P.I, sm, cta, ncta, ns);
+    const EpiResidual ed{L.wd, P.h, D};
+    prefetch_phase(ed, P.I, D, cta, ncta, P.pref_bytes);
+    if (!grid_barrier(P.bar_count, P.bar_epoch, P.err)) return;
+
+    // ---- down_proj + residual (pipeline.js:73-74)
+    gemv_phase<EpiResidual, M>(ed, GemvIn{P.mid, P.I, P.m_rows, nullptr, 0.f}, D, sm, cta, ncta, ns);
+    if (l + 1 < P.n_layers) {
+      const LayerW Ln = P.layers[l + 1];
+      const EpiQKV<KT> en{Ln.wq, Ln.wk, Ln.wv, nullptr, nullptr, nullptr, P.NQ, P.KVH, P.HD, P.log2_half};
+      prefetch_phase(en, D, qkv_units, cta, ncta, P.pref_bytes);
+    } else if (P.lm_head) {
+      const EpiArgmax<M> ep{P.lm_head, P.V, nullptr};
+      prefetch_phase(ep, D, P.V, cta, ncta, P.pref_bytes);
+    }
+    if (!grid_barrier(P.bar_count, P.bar_epoch, P.err)) return;
+  }
+
+  if (P.lm_head) {
+    // ---- sampleLast: rmsnorm(model.norm) -> LM head -> argmax (pipeline.js:147-169)
+    float* logits = nullptr;
+    if (P.logits) {
+      const int step = P.step_count ? *P.step_count : 0;
+      if (step < P.logits_cap) logits = P.logits + (size_t)step * M * P.V;
+    }
+    const EpiArgmax<M> ea{P.lm_head, P.V, logits};
+    typename EpiArgmax<M>::State st;
+#pragma unroll
+    for (int i = 0; i < M; ++i) st.key[i] = 0ull;
+    gemv_phase<EpiArgmax<M>, M>(ea, GemvIn{P.h, D, P.m_rows, P.final_norm, P.eps}, P.V, sm, cta, ncta, st);
+    if (threadIdx.x < M) sbest[threadIdx.x] = 0ull;
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < M; ++i)
+      if (st.key[i]) atomicMax(&sbest[i], st.key[i]);
+    __syncthreads();
+    if (threadIdx.x < P.m_rows && sbest[threadIdx.x]) atomicMax(&P.best[threadIdx.x], sbest[threadIdx.x]);
+    if (!grid_barrier(P.bar_count, P.bar_epoch, P.err)) return;
+    if (cta == 0) {
+      if (threadIdx.x < P.m_rows) {
+        const int m = threadIdx.x;
+        const unsigned long long k = atomicExch(&P.best[m], 0ull);
+        const int tok = argmax_key_index(k);
+        P.tokens_out[m] = tok;
+        if (P.history) {
+          const int step = P.step_count ? *P.step_count : 0;
+          if (step < P.hist_cap) P.history[(size_t)step * P.m_rows + m] = tok;
+        }
+        if (P.advance_rows) {
+          P.rows[m].pos += 1;
+          P.rows[m].slot += 1;
+        }
+      }
+      __syncthreads();
+      if (threadIdx.x == 0 && P.step_count) atomicAdd(P.step_count, 1);
+    }
+  } else if (P.advance_rows && cta == 0 && threadIdx.x < P.m_rows) {
+    P.rows[threadIdx.x].pos += 1;
+    P.rows[threadIdx.x].slot += 1;
+  }
+}
+
+template <typename KT, int HD, int M>
+static cudaError_t launch_one(const StageParams& p, int grid, cudaStream_t st) {
+  auto fn = stage_kernel<KT, HD, M>;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kStageSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, fn, p);
+}
+
+template <typename KT, int HD>
+static cudaError_t launch_m(const StageParams& p, int grid, cudaStream_t st) {
+  if (p.m_rows <= 1) return launch_one<KT, HD, 1>(p, grid, st);
+  if (p.m_rows <= 2) return launch_one<KT, HD, 2>(p, grid, st);
+  if (p.m_rows <= 4) return launch_one<KT, HD, 4>(p, grid, st);
+  return launch_one<KT, HD, 8>(p, grid, st);
+}
+
+template <typename KT, int HD>
+static cudaError_t configure_hd() {
+  const int bytes = (int)kStageSmemBytes;
+  cudaError_t e = cudaFuncSetAttribute(stage_kernel<KT, HD, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(stage_kernel<KT, HD, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(stage_kernel<KT, HD, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(stage_kernel<KT, HD, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  return e;
+}
+
+}  // namespace dllm

@@ -1,0 +1,111 @@
+"""End-to-end parity of the decode token loop (pipeline.js:255-281) on the
+Qwen2.5-0.5B architecture: random-init bf16 weights N(0,0.02), norms 1.0,
+seed 0, 16 prompt ids uniform in [0, vocab), 32 greedy tokens.
+
+Bar: identical greedy tokens for all 32 steps, logits within rtol 2e-2 /
+atol 2e-2 at every step (fp32 accumulation), against the oracle. fp32 KV is the
+reference's own precision; the bf16 KV cache is compared with the oracle in its
+bf16-KV mode (same storage rounding) for tokens, and with the fp32 oracle for
+logits within the same tolerance."""
+import numpy as np
+import pytest
+
+import ref_forward as ref
+import synth
+from helpers import assert_close, build_leader, get_weights, oracle_cfg, top2_margin
+
+pytestmark = pytest.mark.gpu
+
+STEPS = 32
+
+
+@pytest.fixture(scope="module")
+def w05(weights_cache):
+    cfg = oracle_cfg("0.5b", max_pos=128)
+    return cfg, get_weights(weights_cache, "0.5b", cfg)
+
+
+@pytest.fixture(scope="module")
+def oracle_runs(w05):
+    cfg, W = w05
+    prompt = synth.prompt_tokens(cfg, 16, seed=0)
+    runs = {}
+    for kv in ("f32", "bf16"):
+        o = ref.OracleLeader(cfg, ref.Weights(W), kv_dtype=kv)
+        runs[kv] = o.generate(prompt, STEPS, keep_logits=True)
+    return prompt, runs
+
+
+@pytest.mark.parametrize("kv_dtype", ["f32", "bf16"])
+def test_generate_32_tokens(dllm, w05, oracle_runs, kv_dtype):
+    cfg, W = w05
+    prompt, runs = oracle_runs
+    want_tokens, want_logits = runs[kv_dtype]
+    ctx, ld = build_leader(dllm, cfg, W, kv_dtype)
+    ld.set_keep_logits(STEPS)
+    got = []
+    ld.onToken = got.append
+    last = ld.generate(prompt, STEPS)
+    assert last == got[-1]
+    margins = [top2_margin(l) for l in want_logits]
+    assert got == want_tokens, (f"first mismatch at step {next(i for i, (a, b) in enumerate(zip(got, want_tokens)) if a != b)}"
+                                f"; oracle top-2 margins {margins}")
+    for i in range(len(got)):
+        lg = ld.read_logits(i)
+        assert_close(lg, want_logits[i], rtol=2e-2, atol=2e-2, what=f"logits step {i}")
+        assert_close(lg, runs["f32"][1][i], rtol=2e-2, atol=2e-2, what=f"logits vs fp32 oracle step {i}")
+    # the fp32 path is much tighter than the bar
+    if kv_dtype == "f32":
+        assert max(float(np.max(np.abs(ld.read_logits(i) - want_logits[i]))) for i in range(len(got))) < 2e-3
+    ld.close()
+    ctx.close()
+
+
+def test_device_decode_matches_generate(dllm, w05, oracle_runs):
+    """The device-resident graph loop (no per-token host round trip) emits the
+    same tokens as generate's per-token loop."""
+    cfg, W = w05
+    prompt, runs = oracle_runs
+    ctx, ld = build_leader(dllm, cfg, W, "f32")
+    ld.generate(prompt, 1)  # prefill only: T0 = 16, first token emitted
+    first = runs["f32"][0][0]
+    toks = ld.decode(first, STEPS - 1)
+    assert toks == runs["f32"][0][1:STEPS]
+    assert ld.stage.T0 == 16 + STEPS - 1
+    ld.close()
+    ctx.close()
+
+
+def test_eos_break(dllm, w05, oracle_runs):
+    """generate stops right after emitting eosTokenId (pipeline.js:263)."""
+    import dataclasses
+    cfg, W = w05
+    prompt, runs = oracle_runs
+    toks = runs["f32"][0]
+    eos = toks[5]
+    k = toks.index(eos)
+    cfg2 = dataclasses.replace(cfg, eos_token_id=eos)
+    ctx, ld = build_leader(dllm, cfg2, W, "f32")
+    got = []
+    ld.onToken = got.append
+    ld.generate(prompt, STEPS)
+    assert got == toks[:k + 1]
+    ld.close()
+    ctx.close()
+
+
+def test_sample_last_and_embed(dllm, w05):
+    cfg, W = w05
+    ctx, ld = build_leader(dllm, cfg, W, "f32")
+    o = ref.OracleLeader(cfg, ref.Weights(W))
+    toks = [0, 1, 151935, 777]
+    np.testing.assert_array_equal(ld.embedTokens(toks), o.embed_tokens(toks).reshape(-1))
+    h = np.random.default_rng(9).standard_normal(cfg.hidden_size, dtype=np.float32)
+    tok, lg = ld.sampleLast(h, return_logits=True)
+    want_tok, want_lg = o.sample_last(h)
+    assert_close(lg, want_lg, rtol=1e-4, atol=1e-5, what="sampleLast logits")
+    assert tok == want_tok
+    with pytest.raises(dllm.DllmError):
+        ld.embedTokens([cfg.vocab_size])
+    ld.close()
+    ctx.close()
