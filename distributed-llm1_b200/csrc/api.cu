@@ -48,6 +48,7 @@ struct dllm_buf {
 };
 
 struct dllm_ctx {
+  int refs = 1;  // the caller's reference + one per live buffer, stage and leader
   int device = 0;
   dllm_config cfg{};
   cudaStream_t own_stream = nullptr;
@@ -141,6 +142,12 @@ int set_err(dllm_ctx* c, int code, const char* fmt, ...) {
     if (e_ != cudaSuccess) return set_err((ctx), DLLM_ECUDA, "%s: %s", #expr, cudaGetErrorString(e_)); \
   } while (0)
 
+void ctx_free(dllm_ctx* c);
+void ctx_retain(dllm_ctx* c) { c->refs += 1; }
+void ctx_release(dllm_ctx* c) {
+  if (c && --c->refs == 0) ctx_free(c);
+}
+
 int use_device(dllm_ctx* c) {
   cudaError_t e = cudaSetDevice(c->device);
   if (e != cudaSuccess) return set_err(c, DLLM_ECUDA, "cudaSetDevice(%d): %s", c->device, cudaGetErrorString(e));
@@ -230,6 +237,7 @@ int new_buf(dllm_ctx* c, size_t n, int dtype, const char* label, dllm_buf** out)
     delete b;
     return set_err(c, DLLM_ECUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
   }
+  ctx_retain(c);
   *out = b;
   return DLLM_OK;
 }
@@ -505,6 +513,26 @@ void rope_table(const dllm_config& f, std::vector<float>* out) {
 
 }  // namespace
 
+namespace {
+void ctx_free(dllm_ctx* c) {
+  if (!c) return;
+  cudaSetDevice(c->device);
+  if (c->stream) cudaStreamSynchronize(c->stream);
+  dev_free(c->freq);
+  dev_free(c->err_dev);
+  dev_free(c->best);
+  dev_free(c->attn.part_o);
+  dev_free(c->attn.part_ml);
+  dev_free(c->attn.arrive);
+  dev_free(c->attn_rows);
+  if (c->err_host) cudaFreeHost(c->err_host);
+  if (c->best_host) cudaFreeHost(c->best_host);
+  if (c->sync_event) cudaEventDestroy(c->sync_event);
+  if (c->own_stream) cudaStreamDestroy(c->own_stream);
+  delete c;
+}
+}  // namespace
+
 // =====================================================================================
 extern "C" {
 
@@ -593,23 +621,9 @@ int dllm_init_kernels(int device, const dllm_config* cfg, dllm_ctx** out) {
   return DLLM_OK;
 }
 
-void dllm_ctx_destroy(dllm_ctx* c) {
-  if (!c) return;
-  cudaSetDevice(c->device);
-  if (c->stream) cudaStreamSynchronize(c->stream);
-  dev_free(c->freq);
-  dev_free(c->err_dev);
-  dev_free(c->best);
-  dev_free(c->attn.part_o);
-  dev_free(c->attn.part_ml);
-  dev_free(c->attn.arrive);
-  dev_free(c->attn_rows);
-  if (c->err_host) cudaFreeHost(c->err_host);
-  if (c->best_host) cudaFreeHost(c->best_host);
-  if (c->sync_event) cudaEventDestroy(c->sync_event);
-  if (c->own_stream) cudaStreamDestroy(c->own_stream);
-  delete c;
-}
+void dllm_ctx_destroy(dllm_ctx* c) { ctx_release(c); }
+
+
 
 const char* dllm_last_error(const dllm_ctx* c) { return c ? c->err.c_str() : "null context"; }
 
@@ -714,7 +728,9 @@ void dllm_buf_free(dllm_buf* b) {
   if (--b->refs > 0) return;
   cudaSetDevice(b->device);
   if (b->ptr) cudaFree(b->ptr);
+  dllm_ctx* c = b->ctx;
   delete b;
+  ctx_release(c);
 }
 
 size_t dllm_buf_bytes(const dllm_buf* b) { return b ? b->bytes : 0; }
@@ -927,6 +943,7 @@ int dllm_stage_create(dllm_ctx* c, int start, int end, dllm_stage** out) {
   if (int rc = use_device(c)) return rc;
   auto* s = new dllm_stage();
   s->ctx = c;
+  ctx_retain(c);
   s->start = start;
   s->end = end;
   s->nl = end - start;
@@ -1007,6 +1024,7 @@ void dllm_stage_destroy(dllm_stage* s) {
   dev_free(s->hbuf);
   dev_free(s->tokbuf);
   delete s;
+  ctx_release(c);
 }
 
 int dllm_stage_set_weight(dllm_stage* s, const char* name, dllm_buf* b) {
@@ -1192,6 +1210,7 @@ int dllm_leader_create(dllm_ctx* c, int start, int end, dllm_leader** out) {
   *out = nullptr;
   auto* ld = new dllm_leader();
   ld->ctx = c;
+  ctx_retain(c);
   int rc = dllm_stage_create(c, start, end, &ld->st);
   if (!rc) rc = use_device(c);
   if (!rc) rc = dev_alloc(c, &ld->tok_dev, dllm::kMaxRows, "tokens");
@@ -1234,7 +1253,9 @@ void dllm_leader_destroy(dllm_leader* ld) {
   dev_free(ld->logits_ring);
   if (ld->pin_in) cudaFreeHost(ld->pin_in);
   if (ld->pin_out) cudaFreeHost(ld->pin_out);
+  dllm_ctx* c = ld->ctx;
   delete ld;
+  ctx_release(c);
 }
 
 dllm_stage* dllm_leader_stage(dllm_leader* ld) { return ld ? ld->st : nullptr; }

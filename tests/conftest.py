@@ -22,3 +22,11 @@ def dllm():
 @pytest.fixture(scope="session")
 def weights_cache():
     return {}
+
+
+@pytest.fixture(autouse=True)
+def _release_device_objects():
+    """Contexts, stages and buffers hold device memory; free them between tests."""
+    yield
+    import gc
+    gc.collect()

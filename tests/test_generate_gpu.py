@@ -50,10 +50,15 @@ def test_generate_32_tokens(dllm, w05, oracle_runs, kv_dtype):
     margins = [top2_margin(l) for l in want_logits]
     assert got == want_tokens, (f"first mismatch at step {next(i for i, (a, b) in enumerate(zip(got, want_tokens)) if a != b)}"
                                 f"; oracle top-2 margins {margins}")
+    # the fp32-KV oracle is the reference's own precision; its token sequence is the
+    # same input only up to (and including) the first step where the two runs differ
+    f32_tokens = runs["f32"][0]
+    same = next((i for i, (a, b) in enumerate(zip(got, f32_tokens)) if a != b), len(got) - 1)
     for i in range(len(got)):
         lg = ld.read_logits(i)
         assert_close(lg, want_logits[i], rtol=2e-2, atol=2e-2, what=f"logits step {i}")
-        assert_close(lg, runs["f32"][1][i], rtol=2e-2, atol=2e-2, what=f"logits vs fp32 oracle step {i}")
+        if i <= same:
+            assert_close(lg, runs["f32"][1][i], rtol=2e-2, atol=2e-2, what=f"logits vs fp32 oracle step {i}")
     # the fp32 path is much tighter than the bar
     if kv_dtype == "f32":
         assert max(float(np.max(np.abs(ld.read_logits(i) - want_logits[i]))) for i in range(len(got))) < 2e-3
