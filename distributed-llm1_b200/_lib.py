@@ -96,6 +96,8 @@ SIGNATURES = {
     "dllm_stage_fill_kv_random": (C.c_int, [P, C.c_int, C.c_int, C.c_uint64]),
     "dllm_stage_set_page_table": (C.c_int, [P, C.c_int, I32P, C.c_int]),
     "dllm_stage_pages_per_seq": (C.c_int, [P]),
+    "dllm_stage_set_trace": (C.c_int, [P, C.c_int]),
+    "dllm_stage_read_trace": (C.c_int, [P, C.POINTER(C.c_uint64), C.c_int]),
     "dllm_leader_create": (C.c_int, [P, C.c_int, C.c_int, PP]),
     "dllm_leader_destroy": (None, [P]),
     "dllm_leader_stage": (P, [P]),

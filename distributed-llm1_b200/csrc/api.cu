@@ -99,6 +99,10 @@ struct dllm_stage {
   float* hbuf = nullptr;
   size_t tokbuf_cap = 0;
   int32_t* tokbuf = nullptr;
+  // tracing: %globaltimer at kernel start and after every grid barrier (last launch)
+  unsigned long long* trace = nullptr;
+  int trace_cap = 0;
+  int version = 0;  // bumped when weights or tracing change (captured graphs rebuild)
 };
 
 struct dllm_leader {
@@ -118,6 +122,7 @@ struct dllm_leader {
   bool last_in_ring = false;
   cudaGraphExec_t g_e2e = nullptr;
   cudaGraphExec_t g_dev = nullptr;
+  int graph_version = -1;          // stage version the graphs were captured for
   int pending_steps = 0;           // steps of the latest decode_enqueue
 };
 
@@ -438,6 +443,8 @@ StageParams base_params(dllm_stage* s) {
   P.bar_epoch = s->bar + 1;
   P.err = c->err_dev;
   P.pref_bytes = kPrefetchBytes;
+  P.trace = s->trace;
+  P.trace_cap = s->trace_cap;
   P.xs_floats = dllm::kStageXsFloats;
   P.part_floats = dllm::kStagePartFloats;
   return P;
@@ -1023,6 +1030,7 @@ void dllm_stage_destroy(dllm_stage* s) {
   dev_free(s->tok);
   dev_free(s->hbuf);
   dev_free(s->tokbuf);
+  dev_free(s->trace);
   delete s;
   ctx_release(c);
 }
@@ -1036,6 +1044,7 @@ int dllm_stage_set_weight(dllm_stage* s, const char* name, dllm_buf* b) {
   if (it != s->W.end()) dllm_buf_free(it->second);
   s->W[name] = b;
   s->dirty = true;
+  s->version += 1;
   return DLLM_OK;
 }
 
@@ -1201,6 +1210,32 @@ int dllm_stage_set_page_table(dllm_stage* s, int seq, const int32_t* pages, int 
 }
 
 int dllm_stage_pages_per_seq(const dllm_stage* s) { return s ? s->pages_per_seq : -1; }
+
+int dllm_stage_set_trace(dllm_stage* s, int cap) {
+  if (!s) return DLLM_EINVAL;
+  dllm_ctx* c = s->ctx;
+  if (cap < 0) return set_err(c, DLLM_EINVAL, "set_trace: negative capacity");
+  if (int rc = use_device(c)) return rc;
+  CK(c, cudaStreamSynchronize(c->stream));
+  dev_free(s->trace);
+  s->trace = nullptr;
+  s->trace_cap = 0;
+  if (cap > 0) {
+    if (int rc = dev_alloc(c, &s->trace, (size_t)cap, "trace")) return rc;
+    s->trace_cap = cap;
+  }
+  s->version += 1;
+  return DLLM_OK;
+}
+
+int dllm_stage_read_trace(dllm_stage* s, uint64_t* out, int cap) {
+  if (!s || !out) return DLLM_EINVAL;
+  dllm_ctx* c = s->ctx;
+  if (cap <= 0 || cap > s->trace_cap) return set_err(c, DLLM_EINVAL, "read_trace: %d of %d entries", cap, s->trace_cap);
+  if (int rc = use_device(c)) return rc;
+  CK(c, cudaMemcpyAsync(out, s->trace, (size_t)cap * 8, cudaMemcpyDeviceToHost, c->stream));
+  return sync_check(c, kDefaultTimeoutMs);
+}
 
 // ---- LeaderPipeline (pipeline.js:91-282) --------------------------------------------------
 void dllm_leader_destroy(dllm_leader* ld);
@@ -1402,8 +1437,10 @@ int dllm_leader_generate(dllm_leader* ld, const int32_t* tokens, int n_tokens, i
   if (int rc = resolve(s)) return rc;
   if (!s->embed) return set_err(c, DLLM_ENOTFOUND, "missing weight model.embed_tokens.weight");
   if (int rc = need_head(s)) return rc;
+  if (ld->graph_version != s->version) drop_graphs(ld);
   if (!ld->g_e2e)
     if (int rc = build_graph(ld, true, &ld->g_e2e)) return rc;
+  ld->graph_version = s->version;
   const int D = f.hidden_size;
   // ---- prefill: forward(embedTokens(tokens), len, 0) then sampleLast (pipeline.js:259-261)
   if (int rc = ensure_hbuf(s, n_tokens)) return rc;
@@ -1456,8 +1493,10 @@ int dllm_leader_decode_enqueue(dllm_leader* ld, int32_t first_token, int steps) 
   if (int rc = resolve(s)) return rc;
   if (!s->embed) return set_err(c, DLLM_ENOTFOUND, "missing weight model.embed_tokens.weight");
   if (int rc = need_head(s)) return rc;
+  if (ld->graph_version != s->version) drop_graphs(ld);
   if (!ld->g_dev)
     if (int rc = build_graph(ld, false, &ld->g_dev)) return rc;
+  ld->graph_version = s->version;
   RowDesc rd{0, s->T0[0], s->T0[0], 0};
   CK(c, cudaMemcpyAsync(ld->dec_rows, &rd, sizeof(rd), cudaMemcpyHostToDevice, c->stream));
   CK(c, cudaMemcpyAsync(ld->tok_dev, &first_token, 4, cudaMemcpyHostToDevice, c->stream));

@@ -49,6 +49,13 @@ DLLM_DEV void prefetch_l2_bulk(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
+// Nanosecond global timer (same clock on every SM).
+DLLM_DEV unsigned long long global_timer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
 // L2-coherent loads for data produced by other CTAs of the same grid.
 DLLM_DEV float ld_cg(const float* p) { return __ldcg(p); }
 

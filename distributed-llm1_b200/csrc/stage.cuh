@@ -52,6 +52,8 @@ struct StageParams {
   unsigned int* bar_epoch;
   int* err;
   int pref_bytes;            // per-CTA L2 prefetch budget for the next phase
+  unsigned long long* trace; // optional: %globaltimer (ns) at kernel start and after every barrier
+  int trace_cap;
   int xs_floats;             // dynamic smem partition
   int part_floats;
 };

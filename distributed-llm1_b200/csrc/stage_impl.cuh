@@ -21,6 +21,12 @@ __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P)
   NoState ns;
   const int D = P.D, QD = P.NQ * P.HD;
   const int qkv_units = (P.NQ + 2 * P.KVH) * (P.HD >> 1);
+  int tr = 0;  // trace slot: CTA 0 stamps the global timer at start and after every barrier
+  auto trace = [&]() {
+    if (P.trace && cta == 0 && threadIdx.x == 0 && tr < P.trace_cap) P.trace[tr] = global_timer_ns();
+    ++tr;
+  };
+  trace();
 
   // Weights never depend on earlier phases: warm L2 for the first matvec.
   if (P.n_layers > 0) {
@@ -48,6 +54,7 @@ __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P)
       }
     }
     if (!grid_barrier(P.bar_count, P.bar_epoch, P.err)) return;
+    trace();
   }
 
   for (int l = 0; l < P.n_layers; ++l) {
@@ -59,24 +66,28 @@ __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P)
     const EpiResidual eo{L.wo, P.h, D};
     prefetch_phase(eo, QD, D, cta, ncta, P.pref_bytes);
     if (!grid_barrier(P.bar_count, P.bar_epoch, P.err)) return;
+    trace();
 
     // ---- attention over slots [0, slot] (pipeline.js:65)
     const AttnArgs A{P.q, P.att, L.kc, L.vc, P.kv, P.rows, P.m_rows, P.NQ, P.KVH, P.scale, P.max_splits,
                      P.part_o, P.part_ml, P.arrive, P.err};
     attn_phase<KT, HD>(A, smem, cta, ncta);
     if (!grid_barrier(P.bar_count, P.bar_epoch, P.err)) return;
+    trace();
 
     // ---- o_proj + residual (pipeline.js:66-67)
     gemv_phase<EpiResidual, M>(eo, GemvIn{P.att, QD, P.m_rows, nullptr, 0.f}, D, sm, cta, ncta, ns);
     const EpiSiluGate eg{L.wg, L.wu, P.mid, P.I};
     prefetch_phase(eg, D, P.I, cta, ncta, P.pref_bytes);
     if (!grid_barrier(P.bar_count, P.bar_epoch, P.err)) return;
+    trace();
 
     // ---- rmsnorm -> gate, up -> siluMul (pipeline.js:69-72)
     gemv_phase<EpiSiluGate, M>(eg, GemvIn{P.h, D, P.m_rows, L.ln2, P.eps}, P.I, sm, cta, ncta, ns);
     const EpiResidual ed{L.wd, P.h, D};
     prefetch_phase(ed, P.I, D, cta, ncta, P.pref_bytes);
     if (!grid_barrier(P.bar_count, P.bar_epoch, P.err)) return;
+    trace();
 
     // ---- down_proj + residual (pipeline.js:73-74)
     gemv_phase<EpiResidual, M>(ed, GemvIn{P.mid, P.I, P.m_rows, nullptr, 0.f}, D, sm, cta, ncta, ns);
@@ -89,6 +100,7 @@ __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P)
       prefetch_phase(ep, D, P.V, cta, ncta, P.pref_bytes);
     }
     if (!grid_barrier(P.bar_count, P.bar_epoch, P.err)) return;
+    trace();
   }
 
   if (P.lm_head) {
@@ -111,6 +123,7 @@ __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P)
     __syncthreads();
     if (threadIdx.x < P.m_rows && sbest[threadIdx.x]) atomicMax(&P.best[threadIdx.x], sbest[threadIdx.x]);
     if (!grid_barrier(P.bar_count, P.bar_epoch, P.err)) return;
+    trace();
     if (cta == 0) {
       if (threadIdx.x < P.m_rows) {
         const int m = threadIdx.x;

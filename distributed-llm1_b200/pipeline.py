@@ -186,6 +186,16 @@ class Stage:
     def fill_kv_random(self, seq: int, n_slots: int, seed: int = 0):
         self.k._check(self.lib.dllm_stage_fill_kv_random(self.handle, seq, n_slots, seed), "fill_kv_random")
 
+    def set_trace(self, cap: int):
+        """Stamp the GPU global timer at kernel start and after every grid barrier."""
+        self.k._check(self.lib.dllm_stage_set_trace(self.handle, cap), "set_trace")
+
+    def read_trace(self, cap: int) -> np.ndarray:
+        out = np.zeros(cap, np.uint64)
+        self.k._check(self.lib.dllm_stage_read_trace(self.handle, out.ctypes.data_as(C.POINTER(C.c_uint64)), cap),
+                      "read_trace")
+        return out
+
     def pages_per_seq(self) -> int:
         return int(self.lib.dllm_stage_pages_per_seq(self.handle))
 

@@ -173,6 +173,13 @@ int dllm_stage_fill_kv_random(dllm_stage* st, int seq, int n_slots, uint64_t see
  * distinct and < max_seqs * pages_per_seq). Test hook for the paged layout. */
 int dllm_stage_set_page_table(dllm_stage* st, int seq, const int32_t* pages, int n_pages);
 int dllm_stage_pages_per_seq(const dllm_stage* st);
+/* Tracing (the reference logs performance.now() deltas, pipeline.js:144,158,172):
+ * with cap > 0 every stage-kernel launch stamps the GPU global timer (ns) at
+ * its start and after each grid barrier into a device buffer of `cap` entries
+ * (0 turns it off). Per decode pass: start, [embed], then 5 per layer (after
+ * QKV, attention, O, gate/up, down), then [head]. Reads the latest launch's. */
+int dllm_stage_set_trace(dllm_stage* st, int cap);
+int dllm_stage_read_trace(dllm_stage* st, uint64_t* out, int cap);
 
 /* ---- LeaderPipeline (pipeline.js:91-282), local stage only ------------------ */
 /* new LeaderPipeline(k, [start,end), ...) (pipeline.js:92-107). */
