@@ -112,6 +112,7 @@ SIGNATURES = {
     "dllm_leader_set_keep_logits": (C.c_int, [P, C.c_int]),
     "dllm_leader_last_logits": (C.c_int, [P, F32P]),
     "dllm_leader_read_logits": (C.c_int, [P, C.c_int, F32P]),
+    "dllm_attention_noalloc": (C.c_int, [P, P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, P]),
 }
 
 _lib = None

@@ -1,6 +1,10 @@
 // ops.cu — op-level kernels behind the ctx API of kernels.js (one launcher per
 // shader) and utility kernels (synthetic weights, KV cache access, argmax).
 // The matvec and attention ops reuse the phase code of the stage kernel.
+#include <cmath>
+#include <mutex>
+
+#include "dllm.h"
 #include "kernels.cuh"
 #include "ops.cuh"
 #include "stage.cuh"
@@ -330,3 +334,104 @@ cudaError_t op_kv_write(const KvLayout& kv, void* pool, int kv_dtype, int seq, i
 }
 
 }  // namespace dllm
+
+// ---- attention without allocation -------------------------------------------------------
+// Scratch of dllm_attention_noalloc: every GPU that loads this library keeps these
+// bytes until the process exits. Calls share it, so calls that overlap on the GPU
+// race; the ticket counters are cleared by each call before its attention kernel.
+namespace dllm {
+
+constexpr size_t kNoAllocScratchBytes = 4u << 20;  // 4 MiB
+constexpr int kNoAllocMaxRows = 64;
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+__global__ void noalloc_attn_init(RowDesc* rows, unsigned int* arrive, int* err, int t0, int n, int kvh) {
+  for (int i = threadIdx.x; i < n; i += blockDim.x) rows[i] = RowDesc{0, t0 + i, t0 + i, 0};
+  for (int i = threadIdx.x; i < n * kvh; i += blockDim.x) arrive[i] = 0u;
+  if (threadIdx.x == 0) *err = 0;
+}
+
+static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+// Byte layout of the scratch for n rows and `splits` attention splits.
+struct NoAllocLayout {
+  size_t rows, arrive, err, part_ml, part_o, total;
+};
+static NoAllocLayout noalloc_layout(int n, int nq, int kvh, int hd, int splits) {
+  NoAllocLayout L;
+  size_t off = 0;
+  L.rows = off;
+  off = align256(off + sizeof(RowDesc) * (size_t)n);
+  L.arrive = off;
+  off = align256(off + sizeof(unsigned int) * (size_t)n * kvh);
+  L.err = off;
+  off = align256(off + sizeof(int));
+  L.part_ml = off;
+  off = align256(off + sizeof(float) * 2 * (size_t)n * nq * splits);
+  L.part_o = off;
+  off = align256(off + sizeof(float) * (size_t)n * nq * splits * hd);
+  L.total = off;
+  return L;
+}
+
+struct NoAllocDevice {
+  bool ready = false;
+  unsigned char* scratch = nullptr;  // device address of g_noalloc_scratch
+  int sms = 0;
+};
+static NoAllocDevice g_noalloc_dev[kNoAllocMaxDevices];
+static std::mutex g_noalloc_mu;
+
+}  // namespace dllm
+
+extern "C" int dllm_attention_noalloc(const float* q, const float* kcache, const float* vcache, float* out, int t0,
+                                      int n, int num_q_heads, int num_kv_heads, int head_dim, int max_pos,
+                                      void* cuda_stream) {
+  using namespace dllm;
+  if (!q || !kcache || !vcache || !out) return DLLM_EINVAL;
+  if (n < 1 || t0 < 0 || max_pos < 1 || (long long)t0 + n > max_pos) return DLLM_EINVAL;
+  if (head_dim != 64 && head_dim != 128) return DLLM_EINVAL;
+  if (num_kv_heads < 1 || num_q_heads < 1 || num_q_heads % num_kv_heads || num_q_heads / num_kv_heads > kGMax)
+    return DLLM_EINVAL;
+  if (n > kNoAllocMaxRows) return DLLM_ERANGE;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return DLLM_ECUDA;
+  NoAllocDevice& D = g_noalloc_dev[dev];
+  {
+    // once per device, with that device current: resolve the device address of the
+    // static scratch and raise the attention kernel's shared-memory limit
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!D.ready) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return DLLM_ECUDA;
+      int sms = 0;
+      if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
+        return DLLM_ECUDA;
+      if (configure_op_kernels() != cudaSuccess) return DLLM_ECUDA;
+      D.scratch = static_cast<unsigned char*>(p);
+      D.sms = sms;
+      D.ready = true;
+    }
+  }
+  int splits = D.sms / ((n < 8 ? n : 8) * num_kv_heads);
+  if (splits > 64) splits = 64;
+  if (splits < 1) splits = 1;
+  NoAllocLayout L = noalloc_layout(n, num_q_heads, num_kv_heads, head_dim, splits);
+  while (L.total > kNoAllocScratchBytes && splits > 1) L = noalloc_layout(n, num_q_heads, num_kv_heads, head_dim, --splits);
+  if (L.total > kNoAllocScratchBytes) return DLLM_ERANGE;
+  cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+  RowDesc* rows = reinterpret_cast<RowDesc*>(D.scratch + L.rows);
+  unsigned int* arrive = reinterpret_cast<unsigned int*>(D.scratch + L.arrive);
+  int* err = reinterpret_cast<int*>(D.scratch + L.err);
+  noalloc_attn_init<<<1, 256, 0, st>>>(rows, arrive, err, t0, n, num_kv_heads);
+  if (cudaGetLastError() != cudaSuccess) return DLLM_ECUDA;
+  AttnScratch sc{reinterpret_cast<float*>(D.scratch + L.part_o), reinterpret_cast<float*>(D.scratch + L.part_ml), arrive,
+                 splits};
+  const float scale = (float)(1.0 / std::sqrt((double)head_dim));
+  if (op_attention(q, kcache, vcache, out, rows, n, num_q_heads, num_kv_heads, head_dim, max_pos, scale, sc, err,
+                   D.sms, st) != cudaSuccess)
+    return DLLM_ECUDA;
+  return DLLM_OK;
+}

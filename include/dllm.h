@@ -219,6 +219,26 @@ int dllm_leader_last_logits(dllm_leader* ld, float* out);
 /* Logits of kept step `index` (0 = the prefill's sample) of the latest call. */
 int dllm_leader_read_logits(dllm_leader* ld, int index, float* out);
 
+/* ---- attention that allocates nothing ---------------------------------------
+ * No counterpart in the reference. For callers that must not allocate device
+ * memory: a host that owns the whole HBM budget through its own pool and forbids
+ * allocations after start-up, or a latency-critical loop that cannot afford
+ * cudaMalloc/cudaFree (which may synchronise the device). Same math as
+ * dllm_attention (kernels.js:86-132 semantics; caches [max_pos, KVH*HD] fp32,
+ * row t attends slots [0, t0+t]), but the caller passes every buffer as a device
+ * pointer and the split partials, ticket counters and row descriptors live in a
+ * 4 MiB static device array that every GPU loading this library holds until the
+ * process exits. No ctx is needed; work is enqueued on `cuda_stream` (NULL: the
+ * legacy default stream) and the call does not wait for it.
+ * The first call on a device, with that device current, resolves the array's
+ * device address and sets the kernel's shared-memory limit; make that first call
+ * before any latency-sensitive work. Calls share the array: calls that overlap
+ * on the GPU (other streams, other threads) race. Limits: 1 <= n <= 64 rows
+ * (DLLM_ERANGE beyond), head_dim 64 or 128, at most 8 query heads per KV head
+ * (DLLM_EINVAL otherwise). */
+int dllm_attention_noalloc(const float* q, const float* kcache, const float* vcache, float* out, int t0, int n,
+                           int num_q_heads, int num_kv_heads, int head_dim, int max_pos, void* cuda_stream);
+
 #ifdef __cplusplus
 }
 #endif
