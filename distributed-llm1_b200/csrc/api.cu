@@ -31,7 +31,7 @@ using dllm::StageParams;
 namespace {
 
 constexpr int kDefaultTimeoutMs = 15000;  // readF32's limit (kernels.js:201-207)
-constexpr int kMaxSplitsAlloc = 64;       // attention splits per (row, kv head), allocation bound
+constexpr int kMaxSplitsAlloc = dllm::kAttnMaxSplits;  // attention splits per (row, kv head)
 constexpr int kPrefetchBytes = 96 * 1024; // per-CTA L2 prefetch budget between phases
 
 }  // namespace

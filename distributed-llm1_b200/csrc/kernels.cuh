@@ -28,10 +28,17 @@ namespace dllm {
 
 constexpr int kThreads = 512;            // 16 warps per CTA, one CTA per SM
 constexpr int kWarps = kThreads / 32;
-constexpr int kU = 8;                    // 16-byte chunks per lane per task
-constexpr int kSegChunks = 32 * kU;      // 16-byte chunks per task segment (2048 bf16)
-constexpr int kSegElems = kSegChunks * 8;
+// 16-byte weight vectors each lane keeps in flight per task: 16 for single-row
+// units, 8 per row for row pairs (16 either way), i.e. 8 KB per warp.
+template <int R>
+struct Seg {
+  static constexpr int U = 16 / R;
+  static constexpr int Chunks = 32 * U;  // 16-byte chunks per task segment
+  static constexpr int Elems = Chunks * 8;
+};
+constexpr int kSegElemsMax = Seg<1>::Elems;
 constexpr int kGMax = 8;                 // max query heads per KV head
+constexpr int kAttnMaxSplits = 64;       // max attention splits per (row, kv head)
 constexpr int kMaxRows = 8;              // max rows (sequences or prompt tokens) per pass
 
 // ---- block helpers ---------------------------------------------------------------
@@ -51,12 +58,24 @@ DLLM_DEV unsigned int ld_acquire_u32(const unsigned int* p) {
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+// GPU-scope atomic add that releases this thread's earlier writes (and, through a
+// preceding __syncthreads, the CTA's) and acquires the writes released to it.
+DLLM_DEV unsigned int atom_add_acq_rel_u32(unsigned int* p, unsigned int v) {
+  unsigned int r;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(r) : "l"(p), "r"(v) : "memory");
+  return r;
+}
+DLLM_DEV void st_release_u32(unsigned int* p, unsigned int v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
 // Grid-wide barrier for a cooperative (all-CTAs-resident) launch. Sense is kept
 // by a monotonically increasing epoch, so no reset between launches is needed.
-// The wait is bounded: after ~2^33 SM cycles (seconds) the CTA records an error
-// and the caller leaves the kernel; the host reads the flag. Returns false on
-// timeout.
+// One thread per CTA arrives with a release/acquire atomic after __syncthreads
+// (so the whole CTA's writes are published), the last arrival resets the count
+// and releases the next epoch, the others spin on an acquire load. The wait is
+// bounded: after ~2^33 SM cycles (seconds) the CTA records an error and the
+// caller leaves the kernel; the host reads the flag. Returns false on timeout.
 constexpr long long kBarrierTimeoutCycles = 1ll << 33;
 constexpr int kErrBarrier = 2;
 constexpr int kErrKvRange = 3;
@@ -67,13 +86,11 @@ DLLM_DEV bool grid_barrier(unsigned int* count, unsigned int* epoch, int* err) {
   __shared__ int s_ok;
   if (threadIdx.x == 0) {
     const unsigned int e = ld_acquire_u32(epoch);
-    __threadfence();
-    const unsigned int t = atomicAdd(count, 1u);
+    const unsigned int t = atom_add_acq_rel_u32(count, 1u);
     int ok = 1;
     if (t == gridDim.x - 1) {
       atomicExch(count, 0u);
-      __threadfence();
-      atomicAdd(epoch, 1u);
+      st_release_u32(epoch, e + 1u);
     } else {
       const long long t0 = clock64();
       while (ld_acquire_u32(epoch) == e) {
@@ -82,10 +99,8 @@ DLLM_DEV bool grid_barrier(unsigned int* count, unsigned int* epoch, int* err) {
           ok = 0;
           break;
         }
-        __nanosleep(64);
       }
     }
-    __threadfence();
     s_ok = ok;
   }
   __syncthreads();
@@ -166,6 +181,9 @@ template <class Epi, int M>
 DLLM_DEV void gemv_phase(const Epi& epi, const GemvIn& in, int units, const PhaseSmem& sm, int cta, int ncta,
                          typename Epi::State& st) {
   constexpr int R = Epi::R;
+  constexpr int kU = Seg<R>::U;
+  constexpr int kSegChunks = Seg<R>::Chunks;
+  constexpr int kSegElems = Seg<R>::Elems;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int K = in.K, Kc = K >> 3;
   const int u0 = (int)(((long long)cta * units) / ncta);
@@ -457,9 +475,12 @@ struct AttnArgs {
   int* err;
 };
 
-DLLM_DEV int attn_splits(int T, int max_splits, int* chunk_out) {
-  int ns = (T + 31) / 32;
+// Splits of a row's slots [0, T): each split is a multiple of 32 slots and is
+// worked on by `nsub` warps per query head (32 slots each per round).
+DLLM_DEV int attn_splits(int T, int max_splits, int nsub, int* chunk_out) {
+  int ns = (T + 32 * nsub - 1) / (32 * nsub);
   if (ns > max_splits) ns = max_splits;
+  if (ns > kAttnMaxSplits) ns = kAttnMaxSplits;
   if (ns < 1) ns = 1;
   int chunk = (T + ns - 1) / ns;
   chunk = (chunk + 31) & ~31;
@@ -474,6 +495,9 @@ struct KvVec16;
 template <>
 struct KvVec16<float> {
   static constexpr int N = 4;
+  DLLM_DEV static void unpack(uint4 t, float (&v)[4]) {
+    v[0] = __uint_as_float(t.x); v[1] = __uint_as_float(t.y); v[2] = __uint_as_float(t.z); v[3] = __uint_as_float(t.w);
+  }
   DLLM_DEV static void load(const float* p, float (&v)[4]) {
     const float4 t = __ldcg(reinterpret_cast<const float4*>(p));
     v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
@@ -482,6 +506,10 @@ struct KvVec16<float> {
 template <>
 struct KvVec16<__nv_bfloat16> {
   static constexpr int N = 8;
+  DLLM_DEV static void unpack(uint4 t, float (&v)[8]) {
+    v[0] = bf16_lo(t.x); v[1] = bf16_hi(t.x); v[2] = bf16_lo(t.y); v[3] = bf16_hi(t.y);
+    v[4] = bf16_lo(t.z); v[5] = bf16_hi(t.z); v[6] = bf16_lo(t.w); v[7] = bf16_hi(t.w);
+  }
   DLLM_DEV static void load(const __nv_bfloat16* p, float (&v)[8]) {
     const uint4 t = __ldcg(reinterpret_cast<const uint4*>(p));
     v[0] = bf16_lo(t.x); v[1] = bf16_hi(t.x); v[2] = bf16_lo(t.y); v[3] = bf16_hi(t.y);
@@ -514,137 +542,139 @@ DLLM_DEV void load_vec2<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[2]) {
   v[0] = bf16_lo(t); v[1] = bf16_hi(t);
 }
 
-// Attention for one work item; called by the whole CTA. smem needs
-// kGMax*HD (q) + kWarps*kGMax*32 (p) + kWarps*kGMax*(HD+2) (warp combine) floats.
+// Shared-memory floats attn_item needs (q of the group, per-warp softmax
+// numerators, per-warp partial results).
+template <int HD>
+constexpr int attn_smem_floats() {
+  return kGMax * HD + kWarps * 32 + 2 * kWarps + kWarps * HD + 2 * kGMax * kAttnMaxSplits + kGMax;
+}
+
+// Attention for one work item (row m, kv head g, split s); called by the whole
+// CTA. Warp w takes query head h = w % G of the group and the sub-chunks
+// c = w / G, c + nsub, ... of 32 slots: the q.k pass has one lane per slot and
+// reads the slot's K row with 16-byte loads issued before use; the p.V pass has
+// one lane per HD/32 dims. Sub-chunks of a head are combined in shared memory.
 template <typename KT, int HD>
 DLLM_DEV void attn_item(const AttnArgs& A, int m, int g, int s, int nsplit, int chunk, float* smem) {
   constexpr int DPL = HD / 32;  // dims per lane in p.V
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int G = A.NQ / A.KVH;
+  const int nsub = max(1, nwarps / G);
   const RowDesc rd = A.rows[m];
   const int T = rd.slot + 1;
   const int p0 = s * chunk, p1 = min(T, p0 + chunk);
-  float* qs = smem;                          // [kGMax][HD]
-  float* ps = qs + kGMax * HD;               // [kWarps][kGMax][32]
-  float* wm = ps + kWarps * kGMax * 32;      // [kWarps][kGMax]
-  float* wl = wm + kWarps * kGMax;           // [kWarps][kGMax]
-  float* wacc = wl + kWarps * kGMax;         // [kWarps][kGMax][HD]
+  float* qs = smem;                  // [G][HD]
+  float* ps = qs + kGMax * HD;       // [nwarps][32]
+  float* wm = ps + kWarps * 32;      // [nwarps]
+  float* wl = wm + kWarps;           // [nwarps]
+  float* wacc = wl + kWarps;         // [nwarps][HD]
+  float* mrg = wacc + kWarps * HD;   // split merge: [G][nsplit] maxima, [G][nsplit] weights, [G]
 
   const float* qrow = A.q + (size_t)m * A.NQ * HD + (size_t)g * G * HD;
   for (int i = threadIdx.x; i < G * HD; i += blockDim.x) qs[i] = __ldcg(qrow + i);
   __syncthreads();
 
-  float mrun[kGMax], lsum[kGMax], acc[kGMax][DPL];
+  const int h = warp % G, c = warp / G;
+  float mrun = -INFINITY, lsum = 0.f, acc[DPL];
 #pragma unroll
-  for (int h = 0; h < kGMax; ++h) {
-    mrun[h] = -INFINITY;
-    lsum[h] = 0.f;
-#pragma unroll
-    for (int d = 0; d < DPL; ++d) acc[h][d] = 0.f;
-  }
+  for (int d = 0; d < DPL; ++d) acc[d] = 0.f;
   const KT* kc = reinterpret_cast<const KT*>(A.kc);
   const KT* vc = reinterpret_cast<const KT*>(A.vc);
-  float* myps = ps + warp * kGMax * 32;
+  float* myps = ps + warp * 32;
+  const float* qh = qs + h * HD;
 
-  for (int base = p0 + warp * 32; base < p1; base += nwarps * 32) {
-    // slots base..base+31 share one KV page (pages hold >= 32 slots, base % 32 == 0)
-    const long long off0 = A.kv.offset(rd.seq, base, g);
-    const int pos = base + lane;
-    const bool valid = pos < p1;
-    float sc[kGMax];
+  if (c < nsub) {
+    for (int base = p0 + c * 32; base < p1; base += nsub * 32) {
+      // slots base..base+31 share one KV page (pages hold >= 32 slots, base % 32 == 0)
+      const long long off0 = A.kv.offset(rd.seq, base, g);
+      const int pos = base + lane;
+      const bool valid = pos < p1;
+      float sc = 0.f;
+      if (valid) {
+        constexpr int VE = KvVec16<KT>::N;
+        constexpr int NV = HD / VE;
+        constexpr int NB = NV < 16 ? NV : 16;
+        const KT* kr = kc + off0 + (long long)lane * A.kv.row_stride;
 #pragma unroll
-    for (int h = 0; h < kGMax; ++h) sc[h] = 0.f;
-    if (valid) {
-      constexpr int VE = KvVec16<KT>::N;
-      const KT* kr = kc + off0 + (long long)lane * A.kv.row_stride;
-#pragma unroll 4
-      for (int d = 0; d < HD; d += VE) {
-        float kv[VE];
-        KvVec16<KT>::load(kr + d, kv);
+        for (int b0 = 0; b0 < NV; b0 += NB) {
+          uint4 raw[NB];
 #pragma unroll
-        for (int h = 0; h < kGMax; ++h) {
-          if (h < G) {
-            const float* qh = qs + h * HD + d;
+          for (int v = 0; v < NB; ++v) raw[v] = __ldcg(reinterpret_cast<const uint4*>(kr + (b0 + v) * VE));
 #pragma unroll
-            for (int e = 0; e < VE; ++e) sc[h] = fmaf(qh[e], kv[e], sc[h]);
+          for (int v = 0; v < NB; ++v) {
+            float kv[VE];
+            KvVec16<KT>::unpack(raw[v], kv);
+#pragma unroll
+            for (int e = 0; e < VE; ++e) sc = fmaf(qh[(b0 + v) * VE + e], kv[e], sc);
           }
         }
       }
-    }
-    float alpha[kGMax];
+      const float sv = valid ? __fmul_rn(sc, A.scale) : -INFINITY;
+      const float mnew = fmaxf(mrun, warp_max(sv));
+      const float alpha = (mrun == -INFINITY) ? 0.f : expf(mrun - mnew);
+      const float pv = valid ? expf(sv - mnew) : 0.f;
+      lsum = fmaf(lsum, alpha, pv);
+      mrun = mnew;
+      myps[lane] = pv;
+      __syncwarp();
 #pragma unroll
-    for (int h = 0; h < kGMax; ++h) {
-      if (h < G) {
-        const float sv = valid ? __fmul_rn(sc[h], A.scale) : -INFINITY;
-        const float mx = warp_max(sv);
-        const float mnew = fmaxf(mrun[h], mx);
-        alpha[h] = (mrun[h] == -INFINITY) ? 0.f : expf(mrun[h] - mnew);
-        const float pv = valid ? expf(sv - mnew) : 0.f;
-        lsum[h] = fmaf(lsum[h], alpha[h], pv);
-        mrun[h] = mnew;
-        myps[h * 32 + lane] = pv;
-      }
-    }
-    __syncwarp();
-    const int npos = min(32, p1 - base);
+      for (int d = 0; d < DPL; ++d) acc[d] *= alpha;
+      const int npos = min(32, p1 - base);
+      const KT* vbase = vc + off0 + lane * DPL;
+      constexpr int PB = 16;  // V rows in flight per batch
+      for (int j0 = 0; j0 < npos; j0 += PB) {
+        float vv[PB][DPL];
 #pragma unroll
-    for (int h = 0; h < kGMax; ++h)
+        for (int jj = 0; jj < PB; ++jj) {
+          if (j0 + jj < npos) {
+            if constexpr (DPL == 4) load_vec4<KT>(vbase + (long long)(j0 + jj) * A.kv.row_stride, vv[jj]);
+            else load_vec2<KT>(vbase + (long long)(j0 + jj) * A.kv.row_stride, vv[jj]);
+          } else {
 #pragma unroll
-      for (int d = 0; d < DPL; ++d) acc[h][d] *= (h < G) ? alpha[h] : 1.f;
-    const KT* vbase = vc + off0 + lane * DPL;
-#pragma unroll 4
-    for (int j = 0; j < npos; ++j) {
-      float vv[DPL];
-      if constexpr (DPL == 4) load_vec4<KT>(vbase + (long long)j * A.kv.row_stride, vv);
-      else load_vec2<KT>(vbase + (long long)j * A.kv.row_stride, vv);
+            for (int d = 0; d < DPL; ++d) vv[jj][d] = 0.f;
+          }
+        }
 #pragma unroll
-      for (int h = 0; h < kGMax; ++h) {
-        if (h < G) {
-          const float pj = myps[h * 32 + j];
+        for (int jj = 0; jj < PB; ++jj) {
+          const float pj = (j0 + jj < npos) ? myps[j0 + jj] : 0.f;
 #pragma unroll
-          for (int d = 0; d < DPL; ++d) acc[h][d] = fmaf(pj, vv[d], acc[h][d]);
+          for (int d = 0; d < DPL; ++d) acc[d] = fmaf(pj, vv[jj][d], acc[d]);
         }
       }
-    }
-    __syncwarp();
-  }
-  // warp results -> smem
-#pragma unroll
-  for (int h = 0; h < kGMax; ++h) {
-    if (h < G) {
-      const float l = warp_sum(lsum[h]);
-      if (lane == 0) {
-        wm[warp * kGMax + h] = mrun[h];
-        wl[warp * kGMax + h] = l;
-      }
-#pragma unroll
-      for (int d = 0; d < DPL; ++d) wacc[((size_t)warp * kGMax + h) * HD + lane * DPL + d] = acc[h][d];
+      __syncwarp();
     }
   }
+  const float l = warp_sum(lsum);
+  if (lane == 0) {
+    wm[warp] = mrun;
+    wl[warp] = l;
+  }
+#pragma unroll
+  for (int d = 0; d < DPL; ++d) wacc[warp * HD + lane * DPL + d] = acc[d];
   __syncthreads();
-  // combine warps: thread per (h, d)
+  // combine the sub-chunks of each head (warps c*G + h): thread per (h, d)
   float* out_row = A.out + (size_t)m * A.NQ * HD + (size_t)g * G * HD;
   for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
-    const int h = i / HD, d = i - h * HD;
+    const int hh = i / HD, d = i - hh * HD;
     float mx = -INFINITY;
-    for (int w = 0; w < nwarps; ++w) mx = fmaxf(mx, wm[w * kGMax + h]);
-    float l = 0.f, o = 0.f;
-    for (int w = 0; w < nwarps; ++w) {
-      const float mw = wm[w * kGMax + h];
+    for (int cc = 0; cc < nsub; ++cc) mx = fmaxf(mx, wm[cc * G + hh]);
+    float lt = 0.f, o = 0.f;
+    for (int cc = 0; cc < nsub; ++cc) {
+      const float mw = wm[cc * G + hh];
       if (mw == -INFINITY) continue;
       const float f = expf(mw - mx);
-      l = fmaf(wl[w * kGMax + h], f, l);
-      o = fmaf(wacc[((size_t)w * kGMax + h) * HD + d], f, o);
+      lt = fmaf(wl[cc * G + hh], f, lt);
+      o = fmaf(wacc[(cc * G + hh) * HD + d], f, o);
     }
     if (nsplit == 1) {
-      out_row[h * HD + d] = __fdiv_rn(o, l);
+      out_row[hh * HD + d] = __fdiv_rn(o, lt);
     } else {
-      const int hq = g * G + h;
+      const int hq = g * G + hh;
       A.part_o[(((size_t)m * A.NQ + hq) * A.max_splits + s) * HD + d] = o;
       if (d == 0) {
         float* ml = A.part_ml + (((size_t)m * A.NQ + hq) * A.max_splits + s) * 2;
         ml[0] = mx;
-        ml[1] = l;
+        ml[1] = lt;
       }
     }
   }
@@ -652,31 +682,57 @@ DLLM_DEV void attn_item(const AttnArgs& A, int m, int g, int s, int nsplit, int 
     __syncthreads();
     return;
   }
-  // last CTA to finish this (row, g) merges the splits
-  __threadfence();
+  // last CTA to finish this (row, g) merges the splits: one acq_rel ticket per CTA
+  // publishes this CTA's partials and, for the last one, acquires everyone's
   __syncthreads();
   __shared__ int s_last;
   if (threadIdx.x == 0) {
-    const unsigned int t = atomicAdd(&A.arrive[m * A.KVH + g], 1u);
+    const unsigned int t = atom_add_acq_rel_u32(&A.arrive[m * A.KVH + g], 1u);
     s_last = (t == (unsigned int)nsplit - 1);
   }
   __syncthreads();
   if (s_last) {
-    __threadfence();
-    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
-      const int h = i / HD, d = i - h * HD;
-      const int hq = g * G + h;
-      const float* ml = A.part_ml + ((size_t)m * A.NQ + hq) * A.max_splits * 2;
-      const float* po = A.part_o + ((size_t)m * A.NQ + hq) * A.max_splits * HD;
+    // split maxima and sums -> shared memory, one parallel pass
+    float* sm_m = mrg;                       // [G][nsplit]
+    float* sm_l = sm_m + kGMax * nsplit;     // [G][nsplit]; becomes the split weights
+    float* sm_den = sm_l + kGMax * nsplit;   // [G]
+    for (int i = threadIdx.x; i < G * nsplit; i += blockDim.x) {
+      const int hh = i / nsplit, k = i - hh * nsplit;
+      const float* ml = A.part_ml + (((size_t)m * A.NQ + g * G + hh) * A.max_splits + k) * 2;
+      sm_m[i] = __ldcg(ml);
+      sm_l[i] = __ldcg(ml + 1);
+    }
+    __syncthreads();
+    // per head (one warp each): max over splits, split weights exp(m_s - max), denominator
+    for (int hh = warp; hh < G; hh += nwarps) {
       float mx = -INFINITY;
-      for (int k = 0; k < nsplit; ++k) mx = fmaxf(mx, __ldcg(ml + 2 * k));
-      float l = 0.f, o = 0.f;
-      for (int k = 0; k < nsplit; ++k) {
-        const float f = expf(__ldcg(ml + 2 * k) - mx);
-        l = fmaf(__ldcg(ml + 2 * k + 1), f, l);
-        o = fmaf(__ldcg(po + (size_t)k * HD + d), f, o);
+      for (int k = lane; k < nsplit; k += 32) mx = fmaxf(mx, sm_m[hh * nsplit + k]);
+      mx = warp_max(mx);
+      float den = 0.f;
+      for (int k = lane; k < nsplit; k += 32) {
+        const float f = expf(sm_m[hh * nsplit + k] - mx);
+        den = fmaf(sm_l[hh * nsplit + k], f, den);
+        sm_l[hh * nsplit + k] = f;
       }
-      out_row[h * HD + d] = __fdiv_rn(o, l);
+      den = warp_sum(den);
+      if (lane == 0) sm_den[hh] = den;
+    }
+    __syncthreads();
+    // out[h][d] = sum_s w[h][s] * o_s[h][d] / den[h]; loads issued in batches of 8
+    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
+      const int hh = i / HD, d = i - hh * HD;
+      const float* po = A.part_o + ((size_t)m * A.NQ + g * G + hh) * A.max_splits * HD + d;
+      const float* wv = sm_l + hh * nsplit;
+      float o = 0.f;
+      for (int k0 = 0; k0 < nsplit; k0 += 8) {
+        float pvv[8];
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) pvv[kk] = (k0 + kk < nsplit) ? __ldcg(po + (size_t)(k0 + kk) * HD) : 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          if (k0 + kk < nsplit) o = fmaf(wv[k0 + kk], pvv[kk], o);
+      }
+      out_row[hh * HD + d] = __fdiv_rn(o, sm_den[hh]);
     }
     if (threadIdx.x == 0) A.arrive[m * A.KVH + g] = 0u;
   }
@@ -695,7 +751,8 @@ DLLM_DEV void attn_phase(const AttnArgs& A, float* smem, int cta, int ncta) {
       continue;
     }
     int chunk;
-    const int ns = attn_splits(rd.slot + 1, A.max_splits, &chunk);
+    const int nsub = max(1, (int)(blockDim.x >> 5) / (A.NQ / A.KVH));
+    const int ns = attn_splits(rd.slot + 1, A.max_splits, nsub, &chunk);
     const int n_items = A.KVH * ns;
     // items [item, item + n_items) of this row
     for (int j = 0; j < n_items; ++j) {

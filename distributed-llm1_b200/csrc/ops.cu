@@ -148,8 +148,7 @@ cudaError_t op_add_bias(const float* a, const __nv_bfloat16* bias, float* out, i
 // ---- ATTENTION (reference cache layout) -------------------------------------------
 template <int HD>
 constexpr size_t attn_smem_bytes() {
-  return sizeof(float) * ((size_t)kGMax * HD + (size_t)kWarps * kGMax * 32 + 2 * (size_t)kWarps * kGMax +
-                          (size_t)kWarps * kGMax * HD);
+  return sizeof(float) * (size_t)attn_smem_floats<HD>();
 }
 
 template <int HD>

@@ -64,7 +64,7 @@ __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P)
                         reinterpret_cast<KT*>(L.kc), reinterpret_cast<KT*>(L.vc), P.kv, P.rows, P.err};
     gemv_phase<EpiQKV<KT>, M>(eq, GemvIn{P.h, D, P.m_rows, L.ln1, P.eps}, qkv_units, sm, cta, ncta, ns);
     const EpiResidual eo{L.wo, P.h, D};
-    prefetch_phase(eo, QD, D, cta, ncta, P.pref_bytes);
+    prefetch_phase(eo, QD, D, cta, ncta, 2 * P.pref_bytes);
     if (!grid_barrier(P.bar_count, P.bar_epoch, P.err)) return;
     trace();
 

@@ -324,6 +324,18 @@ class OracleLeader:
         h = self.stage.forward(hidden, n, pos_start)
         return h[n - 1]
 
+    def teacher_forced(self, tokens, continuation) -> list[np.ndarray]:
+        """Logits of every step of generate() when the emitted tokens are forced to
+        `continuation` (step i feeds continuation[i-1]): compares a run whose
+        greedy choices differ only at near-ties on identical inputs."""
+        logs = []
+        row = self.forward(self.embed_tokens(tokens), len(tokens), 0)
+        logs.append(self.logits(row))
+        for i in range(1, len(continuation)):
+            row = self.forward(self.embed_tokens([continuation[i - 1]]), 1, len(tokens) + i - 1)
+            logs.append(self.logits(row))
+        return logs
+
     def generate(self, tokens, max_new: int, keep_logits: bool = False):
         """pipeline.js:255-281. Returns (emitted tokens, per-step logits or None)."""
         out, logs = [], []

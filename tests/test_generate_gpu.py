@@ -36,12 +36,12 @@ def oracle_runs(w05):
     return prompt, runs
 
 
-@pytest.mark.parametrize("kv_dtype", ["f32", "bf16"])
-def test_generate_32_tokens(dllm, w05, oracle_runs, kv_dtype):
+def test_generate_32_tokens_fp32_kv(dllm, w05, oracle_runs):
+    """The reference's precision (fp32 KV): identical greedy tokens for 32 steps."""
     cfg, W = w05
     prompt, runs = oracle_runs
-    want_tokens, want_logits = runs[kv_dtype]
-    ctx, ld = build_leader(dllm, cfg, W, kv_dtype)
+    want_tokens, want_logits = runs["f32"]
+    ctx, ld = build_leader(dllm, cfg, W, "f32")
     ld.set_keep_logits(STEPS)
     got = []
     ld.onToken = got.append
@@ -50,18 +50,40 @@ def test_generate_32_tokens(dllm, w05, oracle_runs, kv_dtype):
     margins = [top2_margin(l) for l in want_logits]
     assert got == want_tokens, (f"first mismatch at step {next(i for i, (a, b) in enumerate(zip(got, want_tokens)) if a != b)}"
                                 f"; oracle top-2 margins {margins}")
-    # the fp32-KV oracle is the reference's own precision; its token sequence is the
-    # same input only up to (and including) the first step where the two runs differ
-    f32_tokens = runs["f32"][0]
-    same = next((i for i, (a, b) in enumerate(zip(got, f32_tokens)) if a != b), len(got) - 1)
+    errs = []
     for i in range(len(got)):
         lg = ld.read_logits(i)
         assert_close(lg, want_logits[i], rtol=2e-2, atol=2e-2, what=f"logits step {i}")
-        if i <= same:
-            assert_close(lg, runs["f32"][1][i], rtol=2e-2, atol=2e-2, what=f"logits vs fp32 oracle step {i}")
-    # the fp32 path is much tighter than the bar
-    if kv_dtype == "f32":
-        assert max(float(np.max(np.abs(ld.read_logits(i) - want_logits[i]))) for i in range(len(got))) < 2e-3
+        errs.append(float(np.max(np.abs(lg - want_logits[i]))))
+    assert max(errs) < 2e-3  # the fp32 path is far inside the bar
+    ld.close()
+    ctx.close()
+
+
+def test_generate_32_tokens_bf16_kv(dllm, w05, oracle_runs):
+    """bf16 KV cache: the oracle (bf16-KV mode, and the fp32 reference precision)
+    replays the GPU's own token stream; logits within rtol/atol 2e-2 at every
+    step, and every emitted token is the oracle's argmax except where the
+    oracle's top-2 margin is below that tolerance (a near-tie either may take)."""
+    cfg, W = w05
+    prompt, _ = oracle_runs
+    ctx, ld = build_leader(dllm, cfg, W, "bf16")
+    ld.set_keep_logits(STEPS)
+    got = []
+    ld.onToken = got.append
+    ld.generate(prompt, STEPS)
+    assert len(got) == STEPS
+    for kv in ("bf16", "f32"):
+        forced = ref.OracleLeader(cfg, ref.Weights(W), kv_dtype=kv).teacher_forced(prompt, got)
+        ties = 0
+        for i, want in enumerate(forced):
+            lg = ld.read_logits(i)
+            assert_close(lg, want, rtol=2e-2, atol=2e-2, what=f"logits step {i} vs {kv}-KV oracle")
+            best = ref.argmax_first(want)
+            if got[i] != best:
+                assert top2_margin(want) < 2e-2 and want[got[i]] >= want[best] - 2e-2, f"step {i}: token {got[i]} vs {best}"
+                ties += 1
+        assert ties <= 2
     ld.close()
     ctx.close()
 
