@@ -53,6 +53,9 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-layers", type=int, default=2, help="layers in the CPU baseline sample")
     p.add_argument("--cpu-steps", type=int, default=3, help="tokens in the CPU baseline sample")
+    p.add_argument("--layers", type=int, default=0,
+                   help="profiling case only: run the first N layers + LM head (a few GB on the device); "
+                        "the line is marked and is not the benchmark")
     return p.parse_args()
 
 
@@ -291,6 +294,9 @@ def run_reference(args):
 
 
 def workload_config(args, cfg) -> dict:
+    if getattr(args, "layers", 0):
+        return {"workload": f"PROFILING CASE, not the benchmark: {args.model} dims, first {args.layers} layers + "
+                            f"LM head, {args.kv_len}-slot synthetic bf16 KV, batch 1", "layers": args.layers}
     return {"workload": f"{args.model} greedy decode, {args.kv_len}-slot synthetic bf16 KV per sequence, "
                         f"{'batch 1 on one GPU' if args.gpus == 1 else f'{args.gpus}-stage pipeline, {args.gpus} micro-batches of {args.micro}'}",
             "batch": 1 if args.gpus == 1 else args.gpus * args.micro, "kv_len": args.kv_len,
@@ -304,6 +310,8 @@ def run_single(args):
     dllm = importlib.import_module("distributed-llm1_b200")
     cfg = dllm.PRESETS[args.model].with_(kv_dtype="bf16",
                                          max_pos=args.kv_len + 2 * (args.warmup + args.steps) + 64)
+    if args.layers:
+        cfg = cfg.with_(num_layers=args.layers)
     torch.cuda.set_device(0)
     stream = torch.cuda.Stream()
     ctx = dllm.initKernels(0, cfg)
