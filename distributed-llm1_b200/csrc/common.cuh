@@ -126,7 +126,9 @@ struct RowDesc {
 // seq * max_pages + page when it is null). Element (slot, head, d) is at
 //   phys * page_stride + head * head_stride + (s & (page-1)) * row_stride + d.
 // The reference layout [maxPos, KVH*HD] (pipeline.js:38-43) is the special case
-// log2_page = 0, page_stride = KVH*HD, head_stride = HD.
+// of one page holding every slot: log2_page = 30, row_stride = KVH*HD,
+// head_stride = HD. The stage's own paged cache is head-major inside a page
+// (row_stride = HD), so 32 consecutive slots of one head are contiguous.
 struct KvLayout {
   void* k;
   void* v;
