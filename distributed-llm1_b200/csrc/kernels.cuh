@@ -542,116 +542,76 @@ DLLM_DEV void load_vec2<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[2]) {
   v[0] = bf16_lo(t); v[1] = bf16_hi(t);
 }
 
-// Shared-memory floats attn_item needs (q of the group, per-warp softmax
-// numerators, per-warp partial results).
-template <int HD>
+// Slots of one K/V staging round of an attention item (a multiple of 32).
+constexpr int kAttnRound = 64;
+
+// Shared-memory floats attn_item needs: the K and V rows of one round, the
+// per-warp softmax state and partial outputs, and the split-merge scratch.
+template <typename KT, int HD>
 constexpr int attn_smem_floats() {
-  return kGMax * HD + kWarps * 32 + 2 * kWarps + kWarps * HD + 2 * kGMax * kAttnMaxSplits + kGMax;
+  return (int)(2 * kAttnRound * HD * sizeof(KT) / sizeof(float)) + 2 * kWarps + kWarps * HD +
+         2 * kGMax * kAttnMaxSplits + kGMax;
 }
 
-// Attention for one work item (row m, kv head g, split s); called by the whole
-// CTA. Warp w takes query head h = w % G of the group and the sub-chunks
-// c = w / G, c + nsub, ... of 32 slots: the q.k pass has one lane per slot and
-// reads the slot's K row with 16-byte loads issued before use; the p.V pass has
-// one lane per HD/32 dims. Sub-chunks of a head are combined in shared memory.
-template <typename KT, int HD>
-DLLM_DEV void attn_item(const AttnArgs& A, int m, int g, int s, int nsplit, int chunk, float* smem) {
-  constexpr int DPL = HD / 32;  // dims per lane in p.V
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-  const int G = A.NQ / A.KVH;
-  const int nsub = max(1, nwarps / G);
-  const RowDesc rd = A.rows[m];
-  const int T = rd.slot + 1;
-  const int p0 = s * chunk, p1 = min(T, p0 + chunk);
-  float* qs = smem;                  // [G][HD]
-  float* ps = qs + kGMax * HD;       // [nwarps][32]
-  float* wm = ps + kWarps * 32;      // [nwarps]
-  float* wl = wm + kWarps;           // [nwarps]
-  float* wacc = wl + kWarps;         // [nwarps][HD]
-  float* mrg = wacc + kWarps * HD;   // split merge: [G][nsplit] maxima, [G][nsplit] weights, [G]
+// 16-byte asynchronous copy global -> shared (no register staging), cached in
+// L2 only; completion is awaited with cp_async_wait_all().
+DLLM_DEV void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)),
+               "l"(gsrc)
+               : "memory");
+}
+DLLM_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-  const float* qrow = A.q + (size_t)m * A.NQ * HD + (size_t)g * G * HD;
-  for (int i = threadIdx.x; i < G * HD; i += blockDim.x) qs[i] = __ldcg(qrow + i);
-  __syncthreads();
+// DPL consecutive KV elements (shared memory) -> fp32.
+template <typename KT, int DPL>
+DLLM_DEV void kv_row_part(const KT* p, float (&v)[DPL]);
+template <>
+DLLM_DEV void kv_row_part<__nv_bfloat16, 4>(const __nv_bfloat16* p, float (&v)[4]) {
+  const uint2 t = *reinterpret_cast<const uint2*>(p);
+  v[0] = bf16_lo(t.x); v[1] = bf16_hi(t.x); v[2] = bf16_lo(t.y); v[3] = bf16_hi(t.y);
+}
+template <>
+DLLM_DEV void kv_row_part<__nv_bfloat16, 2>(const __nv_bfloat16* p, float (&v)[2]) {
+  const uint32_t t = *reinterpret_cast<const uint32_t*>(p);
+  v[0] = bf16_lo(t); v[1] = bf16_hi(t);
+}
+template <>
+DLLM_DEV void kv_row_part<float, 4>(const float* p, float (&v)[4]) {
+  const float4 t = *reinterpret_cast<const float4*>(p);
+  v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+}
+template <>
+DLLM_DEV void kv_row_part<float, 2>(const float* p, float (&v)[2]) {
+  const float2 t = *reinterpret_cast<const float2*>(p);
+  v[0] = t.x; v[1] = t.y;
+}
 
-  const int h = warp % G, c = warp / G;
-  float mrun = -INFINITY, lsum = 0.f, acc[DPL];
+// Lane l holds v[0..31] (partial sums for 32 slots); afterwards lane l holds the
+// full sum for slot l. 31 shuffles, fixed order.
+DLLM_DEV float transpose_reduce32(float (&v)[32]) {
+  const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int d = 0; d < DPL; ++d) acc[d] = 0.f;
-  const KT* kc = reinterpret_cast<const KT*>(A.kc);
-  const KT* vc = reinterpret_cast<const KT*>(A.vc);
-  float* myps = ps + warp * 32;
-  const float* qh = qs + h * HD;
-
-  if (c < nsub) {
-    for (int base = p0 + c * 32; base < p1; base += nsub * 32) {
-      // slots base..base+31 share one KV page (pages hold >= 32 slots, base % 32 == 0)
-      const long long off0 = A.kv.offset(rd.seq, base, g);
-      const int pos = base + lane;
-      const bool valid = pos < p1;
-      float sc = 0.f;
-      if (valid) {
-        constexpr int VE = KvVec16<KT>::N;
-        constexpr int NV = HD / VE;
-        constexpr int NB = NV < 16 ? NV : 16;
-        const KT* kr = kc + off0 + (long long)lane * A.kv.row_stride;
+  for (int o = 16; o >= 1; o >>= 1) {
+    const bool up = (lane & o) != 0;
 #pragma unroll
-        for (int b0 = 0; b0 < NV; b0 += NB) {
-          uint4 raw[NB];
-#pragma unroll
-          for (int v = 0; v < NB; ++v) raw[v] = __ldcg(reinterpret_cast<const uint4*>(kr + (b0 + v) * VE));
-#pragma unroll
-          for (int v = 0; v < NB; ++v) {
-            float kv[VE];
-            KvVec16<KT>::unpack(raw[v], kv);
-#pragma unroll
-            for (int e = 0; e < VE; ++e) sc = fmaf(qh[(b0 + v) * VE + e], kv[e], sc);
-          }
-        }
-      }
-      const float sv = valid ? __fmul_rn(sc, A.scale) : -INFINITY;
-      const float mnew = fmaxf(mrun, warp_max(sv));
-      const float alpha = (mrun == -INFINITY) ? 0.f : expf(mrun - mnew);
-      const float pv = valid ? expf(sv - mnew) : 0.f;
-      lsum = fmaf(lsum, alpha, pv);
-      mrun = mnew;
-      myps[lane] = pv;
-      __syncwarp();
-#pragma unroll
-      for (int d = 0; d < DPL; ++d) acc[d] *= alpha;
-      const int npos = min(32, p1 - base);
-      const KT* vbase = vc + off0 + lane * DPL;
-      constexpr int PB = 16;  // V rows in flight per batch
-      for (int j0 = 0; j0 < npos; j0 += PB) {
-        float vv[PB][DPL];
-#pragma unroll
-        for (int jj = 0; jj < PB; ++jj) {
-          if (j0 + jj < npos) {
-            if constexpr (DPL == 4) load_vec4<KT>(vbase + (long long)(j0 + jj) * A.kv.row_stride, vv[jj]);
-            else load_vec2<KT>(vbase + (long long)(j0 + jj) * A.kv.row_stride, vv[jj]);
-          } else {
-#pragma unroll
-            for (int d = 0; d < DPL; ++d) vv[jj][d] = 0.f;
-          }
-        }
-#pragma unroll
-        for (int jj = 0; jj < PB; ++jj) {
-          const float pj = (j0 + jj < npos) ? myps[j0 + jj] : 0.f;
-#pragma unroll
-          for (int d = 0; d < DPL; ++d) acc[d] = fmaf(pj, vv[jj][d], acc[d]);
-        }
-      }
-      __syncwarp();
+    for (int i = 0; i < o; ++i) {
+      const float send = up ? v[i] : v[i + o];
+      const float keep = up ? v[i + o] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
     }
   }
-  const float l = warp_sum(lsum);
-  if (lane == 0) {
-    wm[warp] = mrun;
-    wl[warp] = l;
-  }
-#pragma unroll
-  for (int d = 0; d < DPL; ++d) wacc[warp * HD + lane * DPL + d] = acc[d];
-  __syncthreads();
+  return v[0];
+}
+
+// Tail of an attention item, run by the whole CTA after every warp has written
+// its (max, sum, acc[HD]) to wm/wl/wacc (warp c*G + h holds chunk group c of
+// query head h): combine the groups per head, then either write the output
+// (one split) or the split's partials, take the (row, kv head) ticket, and if
+// this CTA is the last of the splits, merge them all (fixed order).
+template <int HD>
+DLLM_DEV void attn_finish(const AttnArgs& A, int m, int g, int s, int nsplit, int G, int nsub, const float* wm,
+                          const float* wl, const float* wacc, float* mrg) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   // combine the sub-chunks of each head (warps c*G + h): thread per (h, d)
   float* out_row = A.out + (size_t)m * A.NQ * HD + (size_t)g * G * HD;
   for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
@@ -737,6 +697,113 @@ DLLM_DEV void attn_item(const AttnArgs& A, int m, int g, int s, int nsplit, int 
     if (threadIdx.x == 0) A.arrive[m * A.KVH + g] = 0u;
   }
   __syncthreads();
+}
+
+
+// Attention for one work item (row m, kv head g, split s); called by the whole
+// CTA. The item's slots are taken in rounds of kAttnRound: all threads copy the
+// round's K and V rows into shared memory with cp.async (one memory round trip,
+// each row read once for all G query heads), then warp w = c*G + h computes
+// query head h over the round's 32-slot chunk c. q.k: lane l owns dims
+// [DPL*l, DPL*l + DPL) of q_h; the 32 partial dot products are transpose-reduced
+// so lane p holds slot p's score; online softmax per warp; p.V: lane l
+// accumulates its dims. Chunk groups of a head are combined in attn_finish.
+template <typename KT, int HD>
+DLLM_DEV void attn_item(const AttnArgs& A, int m, int g, int s, int nsplit, int chunk, float* smem) {
+  constexpr int DPL = HD / 32;
+  constexpr int VPR = HD * (int)sizeof(KT) / 16;  // 16-byte vectors per K or V row
+  constexpr int CPR = kAttnRound / 32;           // 32-slot chunks per round
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int G = A.NQ / A.KVH;
+  const int nsub = max(1, kWarps / G);
+  const int h = warp % G, c = warp / G;
+  const bool active = c < min(nsub, CPR);
+  const RowDesc rd = A.rows[m];
+  const int T = rd.slot + 1;
+  const int p0 = s * chunk, p1 = min(T, p0 + chunk);
+  KT* ks = reinterpret_cast<KT*>(smem);        // [kAttnRound][HD]
+  KT* vs = ks + kAttnRound * HD;               // [kAttnRound][HD]
+  float* wm = smem + 2 * kAttnRound * HD * sizeof(KT) / sizeof(float);  // [kWarps]
+  float* wl = wm + kWarps;                     // [kWarps]
+  float* wacc = wl + kWarps;                   // [kWarps][HD]
+  float* mrg = wacc + kWarps * HD;             // split merge scratch
+  const KT* kc = reinterpret_cast<const KT*>(A.kc);
+  const KT* vc = reinterpret_cast<const KT*>(A.vc);
+
+  float q[DPL];
+  if (active) {
+    const float* qh = A.q + (size_t)m * A.NQ * HD + (size_t)(g * G + h) * HD + lane * DPL;
+#pragma unroll
+    for (int d = 0; d < DPL; ++d) q[d] = __ldcg(qh + d);
+  }
+  float mrun = -INFINITY, lsum = 0.f, acc[DPL];
+#pragma unroll
+  for (int d = 0; d < DPL; ++d) acc[d] = 0.f;
+
+  for (int base = p0; base < p1; base += kAttnRound) {
+    const int n = min(kAttnRound, p1 - base);
+    __syncthreads();  // readers of the previous round are done
+    // rows [base, base + n): chunk cc of 32 slots lies in one KV page
+    const int nvec = ((n + 31) >> 5) * 32 * VPR;  // per K or V
+    for (int i = threadIdx.x; i < 2 * nvec; i += blockDim.x) {
+      const int which = i >= nvec;
+      const int r = which ? i - nvec : i;
+      const int j = r / VPR, v = r - j * VPR;
+      if (base + j >= p1) continue;
+      const long long off = A.kv.offset(rd.seq, base + (j & ~31), g) + (long long)(j & 31) * A.kv.row_stride;
+      const KT* src = (which ? vc : kc) + off + v * (16 / (int)sizeof(KT));
+      KT* dst = (which ? vs : ks) + j * HD + v * (16 / (int)sizeof(KT));
+      cp_async16(dst, src);
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    if (active) {
+      for (int cc = c; cc * 32 < n; cc += nsub) {
+        const int nvalid = min(32, n - cc * 32);
+        const KT* kr = ks + (cc * 32) * HD + lane * DPL;
+        const KT* vr = vs + (cc * 32) * HD + lane * DPL;
+        float part[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float kv[DPL];
+          kv_row_part<KT, DPL>(kr + j * HD, kv);
+          float sdot = 0.f;
+#pragma unroll
+          for (int d = 0; d < DPL; ++d) sdot = fmaf(q[d], kv[d], sdot);
+          part[j] = sdot;
+        }
+        const float sc = transpose_reduce32(part);  // lane = slot in the chunk
+        const bool valid = lane < nvalid;
+        const float sv = valid ? __fmul_rn(sc, A.scale) : -INFINITY;
+        const float mnew = fmaxf(mrun, warp_max(sv));
+        const float alpha = (mrun == -INFINITY) ? 0.f : expf(mrun - mnew);
+        const float pv = valid ? expf(sv - mnew) : 0.f;
+        lsum = fmaf(lsum, alpha, pv);
+        mrun = mnew;
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) acc[d] *= alpha;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float pj = __shfl_sync(0xffffffffu, pv, j);
+          if (j < nvalid) {  // rows past the item were not copied
+            float vv[DPL];
+            kv_row_part<KT, DPL>(vr + j * HD, vv);
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) acc[d] = fmaf(pj, vv[d], acc[d]);
+          }
+        }
+      }
+    }
+  }
+  const float l = warp_sum(lsum);
+  if (lane == 0) {
+    wm[warp] = active ? mrun : -INFINITY;
+    wl[warp] = active ? l : 0.f;
+  }
+#pragma unroll
+  for (int d = 0; d < DPL; ++d) wacc[warp * HD + lane * DPL + d] = active ? acc[d] : 0.f;
+  __syncthreads();
+  attn_finish<HD>(A, m, g, s, nsplit, G, min(nsub, CPR), wm, wl, wacc, mrg);
 }
 
 // All attention work items of a pass, spread round-robin over the CTAs.

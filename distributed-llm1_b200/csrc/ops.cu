@@ -148,7 +148,7 @@ cudaError_t op_add_bias(const float* a, const __nv_bfloat16* bias, float* out, i
 // ---- ATTENTION (reference cache layout) -------------------------------------------
 template <int HD>
 constexpr size_t attn_smem_bytes() {
-  return sizeof(float) * (size_t)attn_smem_floats<HD>();
+  return sizeof(float) * (size_t)attn_smem_floats<float, HD>();
 }
 
 template <int HD>
