@@ -32,7 +32,10 @@ namespace {
 
 constexpr int kDefaultTimeoutMs = 15000;  // readF32's limit (kernels.js:201-207)
 constexpr int kMaxSplitsAlloc = dllm::kAttnMaxSplits;  // attention splits per (row, kv head)
-constexpr int kPrefetchBytes = 96 * 1024; // per-CTA L2 prefetch budget between phases
+#ifndef DLLM_PREFETCH_BYTES
+#define DLLM_PREFETCH_BYTES (96 * 1024)
+#endif
+constexpr int kPrefetchBytes = DLLM_PREFETCH_BYTES;  // per-CTA L2 prefetch budget between phases
 
 }  // namespace
 

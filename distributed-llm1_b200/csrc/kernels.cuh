@@ -69,31 +69,31 @@ DLLM_DEV void st_release_u32(unsigned int* p, unsigned int v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Grid-wide barrier for a cooperative (all-CTAs-resident) launch. Sense is kept
-// by a monotonically increasing epoch, so no reset between launches is needed.
-// One thread per CTA arrives with a release/acquire atomic after __syncthreads
-// (so the whole CTA's writes are published), the last arrival resets the count
-// and releases the next epoch, the others spin on an acquire load. The wait is
-// bounded: after ~2^33 SM cycles (seconds) the CTA records an error and the
-// caller leaves the kernel; the host reads the flag. Returns false on timeout.
+// Grid-wide barrier for a cooperative (all-CTAs-resident) launch. The counter
+// only grows within a launch (the launcher zeroes it before every launch), so
+// barrier k completes when it reaches k * gridDim.x. After __syncthreads one
+// thread per CTA arrives with a GPU-scope acq_rel atomic add (publishing the
+// CTA's writes); the old value gives this barrier's target; the CTA whose
+// arrival reaches it is released at once, the others poll with acquire loads.
+// One round trip after the last arrival instead of a separate reset and
+// release. The wait is bounded: after ~2^33 SM cycles (seconds) the CTA
+// records an error and the caller leaves the kernel; the host reads the flag.
 constexpr long long kBarrierTimeoutCycles = 1ll << 33;
 constexpr int kErrBarrier = 2;
 constexpr int kErrKvRange = 3;
 constexpr int kErrToken = 4;
 
-DLLM_DEV bool grid_barrier(unsigned int* count, unsigned int* epoch, int* err) {
+DLLM_DEV bool grid_barrier(unsigned int* count, int* err) {
   __syncthreads();
   __shared__ int s_ok;
   if (threadIdx.x == 0) {
-    const unsigned int e = ld_acquire_u32(epoch);
-    const unsigned int t = atom_add_acq_rel_u32(count, 1u);
+    const unsigned int n = gridDim.x;
+    const unsigned int old = atom_add_acq_rel_u32(count, 1u);
+    const unsigned int target = (old / n + 1u) * n;
     int ok = 1;
-    if (t == gridDim.x - 1) {
-      atomicExch(count, 0u);
-      st_release_u32(epoch, e + 1u);
-    } else {
+    if (old + 1u != target) {
       const long long t0 = clock64();
-      while (ld_acquire_u32(epoch) == e) {
+      while ((int)(ld_acquire_u32(count) - target) < 0) {
         if (clock64() - t0 > kBarrierTimeoutCycles) {
           atomicExch(err, kErrBarrier);
           ok = 0;

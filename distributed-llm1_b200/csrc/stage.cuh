@@ -48,8 +48,8 @@ struct StageParams {
   int32_t* history;          // [hist_cap][M] or null
   int hist_cap;
   int advance_rows;          // pos++ and slot++ for every row at the end
-  unsigned int* bar_count;
-  unsigned int* bar_epoch;
+  unsigned int* bar_count;   // grid barrier arrivals, zeroed by launch_stage
+  unsigned int* bar_epoch;   // unused
   int* err;
   int pref_bytes;            // per-CTA L2 prefetch budget for the next phase
   unsigned long long* trace; // optional: %globaltimer (ns) at kernel start and after every barrier

@@ -53,7 +53,7 @@ __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P)
         dst[1] = make_float4(bf16_lo(w.z), bf16_hi(w.z), bf16_lo(w.w), bf16_hi(w.w));
       }
     }
-    if (!grid_barrier(P.bar_count, P.bar_epoch, P.err)) return;
+    if (!grid_barrier(P.bar_count, P.err)) return;
     trace();
   }
 
@@ -65,28 +65,28 @@ __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P)
     gemv_phase<EpiQKV<KT>, M>(eq, GemvIn{P.h, D, P.m_rows, L.ln1, P.eps}, qkv_units, sm, cta, ncta, ns);
     const EpiResidual eo{L.wo, P.h, D};
     prefetch_phase(eo, QD, D, cta, ncta, 2 * P.pref_bytes);
-    if (!grid_barrier(P.bar_count, P.bar_epoch, P.err)) return;
+    if (!grid_barrier(P.bar_count, P.err)) return;
     trace();
 
     // ---- attention over slots [0, slot] (pipeline.js:65)
     const AttnArgs A{P.q, P.att, L.kc, L.vc, P.kv, P.rows, P.m_rows, P.NQ, P.KVH, P.scale, P.max_splits,
                      P.part_o, P.part_ml, P.arrive, P.err};
     attn_phase<KT, HD>(A, smem, cta, ncta);
-    if (!grid_barrier(P.bar_count, P.bar_epoch, P.err)) return;
+    if (!grid_barrier(P.bar_count, P.err)) return;
     trace();
 
     // ---- o_proj + residual (pipeline.js:66-67)
     gemv_phase<EpiResidual, M>(eo, GemvIn{P.att, QD, P.m_rows, nullptr, 0.f}, D, sm, cta, ncta, ns);
     const EpiSiluGate eg{L.wg, L.wu, P.mid, P.I};
     prefetch_phase(eg, D, P.I, cta, ncta, P.pref_bytes);
-    if (!grid_barrier(P.bar_count, P.bar_epoch, P.err)) return;
+    if (!grid_barrier(P.bar_count, P.err)) return;
     trace();
 
     // ---- rmsnorm -> gate, up -> siluMul (pipeline.js:69-72)
     gemv_phase<EpiSiluGate, M>(eg, GemvIn{P.h, D, P.m_rows, L.ln2, P.eps}, P.I, sm, cta, ncta, ns);
     const EpiResidual ed{L.wd, P.h, D};
     prefetch_phase(ed, P.I, D, cta, ncta, P.pref_bytes);
-    if (!grid_barrier(P.bar_count, P.bar_epoch, P.err)) return;
+    if (!grid_barrier(P.bar_count, P.err)) return;
     trace();
 
     // ---- down_proj + residual (pipeline.js:73-74)
@@ -99,7 +99,7 @@ __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P)
       const EpiArgmax<M> ep{P.lm_head, P.V, nullptr};
       prefetch_phase(ep, D, P.V, cta, ncta, P.pref_bytes);
     }
-    if (!grid_barrier(P.bar_count, P.bar_epoch, P.err)) return;
+    if (!grid_barrier(P.bar_count, P.err)) return;
     trace();
   }
 
@@ -122,7 +122,7 @@ __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P)
       if (st.key[i]) atomicMax(&sbest[i], st.key[i]);
     __syncthreads();
     if (threadIdx.x < P.m_rows && sbest[threadIdx.x]) atomicMax(&P.best[threadIdx.x], sbest[threadIdx.x]);
-    if (!grid_barrier(P.bar_count, P.bar_epoch, P.err)) return;
+    if (!grid_barrier(P.bar_count, P.err)) return;
     trace();
     if (cta == 0) {
       if (threadIdx.x < P.m_rows) {
