@@ -136,3 +136,25 @@ def test_sample_last_and_embed(dllm, w05):
         ld.embedTokens([cfg.vocab_size])
     ld.close()
     ctx.close()
+
+
+def test_generate_golden_fixture(dllm):
+    """The CUDA path against the committed golden decode (tests/golden/tiny_decode.npz:
+    oracle tokens and logits, cross-checked with transformers): identical greedy
+    tokens, logits within the parity bar, fp32 KV."""
+    import os
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "tiny_decode.npz")
+    g = np.load(path)
+    cfg = synth.tiny_config(tie_word_embeddings=False)
+    W = synth.synthetic_weights(cfg, seed=int(g["seed"]))
+    ctx, ld = build_leader(dllm, cfg, W, "f32")
+    steps = int(g["steps"])
+    ld.set_keep_logits(steps)
+    got = []
+    ld.onToken = got.append
+    ld.generate([int(t) for t in g["prompt"]], steps)
+    assert got == [int(t) for t in g["tokens"]]
+    for i in range(steps):
+        assert_close(ld.read_logits(i), g["logits"][i], rtol=2e-2, atol=2e-2, what=f"golden logits step {i}")
+    ld.close()
+    ctx.close()

@@ -251,15 +251,28 @@ def test_oracle_vs_transformers_qwen2():
 GOLDEN = os.path.join(ROOT, "tests", "golden", "tiny_decode.npz")
 
 
-def test_golden_fixture():
+def golden():
+    """The committed fixture and its config (tests/golden/make_golden.py)."""
     if not os.path.exists(GOLDEN):
         pytest.skip("golden fixture not generated")
-    g = np.load(GOLDEN)
-    cfg = synth.tiny_config()
+    return np.load(GOLDEN), synth.tiny_config(tie_word_embeddings=False)
+
+
+def test_golden_fixture():
+    """The oracle reproduces the committed greedy decode (tokens and logits)."""
+    g, cfg = golden()
     W = synth.synthetic_weights(cfg, seed=int(g["seed"]))
+    # weights fingerprint: the generator is deterministic
+    assert int(np.sum(W["model.layers.0.self_attn.q_proj.weight"].astype(np.uint64))) == int(g["q0_checksum"])
     o = ref.OracleLeader(cfg, ref.Weights(W))
     toks, logits = o.generate([int(t) for t in g["prompt"]], int(g["steps"]), keep_logits=True)
     assert toks == [int(t) for t in g["tokens"]]
     assert_close(np.stack(logits), g["logits"], rtol=1e-5, atol=1e-6, what="golden logits")
-    # weights fingerprint: the generator is deterministic
-    assert int(np.sum(W["model.layers.0.self_attn.q_proj.weight"].astype(np.uint64))) == int(g["q0_checksum"])
+
+
+def test_golden_fixture_agrees_with_transformers():
+    """The fixture's logits match transformers' Qwen2ForCausalLM (an independent
+    implementation) on the same teacher-forced token stream."""
+    g, _ = golden()
+    assert_close(g["logits"], g["hf_logits"], rtol=1e-3, atol=1e-4, what="oracle vs transformers (golden)")
+    assert [int(t) for t in g["tokens"]] == [int(np.argmax(r)) for r in g["hf_logits"]]
