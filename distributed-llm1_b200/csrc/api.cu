@@ -854,7 +854,7 @@ int dllm_attention(dllm_ctx* c, const dllm_buf* q, const dllm_buf* kcache, const
       return rc;
     if (int rc = dev_alloc(c, &c->attn.part_ml, cap * f.num_q_heads * kMaxSplitsAlloc * 2, "attn partials"))
       return rc;
-    if (int rc = dev_alloc(c, &c->attn.arrive, cap * f.num_kv_heads, "attn tickets")) return rc;
+    if (int rc = dev_alloc(c, &c->attn.arrive, 2 * cap * f.num_kv_heads, "attn tickets")) return rc;
     if (int rc = dev_alloc(c, &c->attn_rows, cap, "attn rows")) return rc;
     c->attn_rows_cap = cap;
   }
@@ -993,7 +993,7 @@ int dllm_stage_create(dllm_ctx* c, int start, int end, dllm_stage** out) {
   if (!rc) rc = dev_alloc(c, &s->mid, R * f.intermediate_size, "mlp");
   if (!rc) rc = dev_alloc(c, &s->part_o, R * f.num_q_heads * kMaxSplitsAlloc * f.head_dim, "attn partials");
   if (!rc) rc = dev_alloc(c, &s->part_ml, R * f.num_q_heads * kMaxSplitsAlloc * 2, "attn partials");
-  if (!rc) rc = dev_alloc(c, &s->arrive, R * f.num_kv_heads, "attn tickets");
+  if (!rc) rc = dev_alloc(c, &s->arrive, 2 * R * f.num_kv_heads, "attn tickets");  // arrivals, finishes
   if (!rc) rc = dev_alloc(c, &s->rows, R, "rows");
   if (!rc) rc = dev_alloc(c, &s->bar, 2, "barrier");
   if (!rc) rc = dev_alloc(c, &s->best, R, "argmax keys");

@@ -471,7 +471,7 @@ struct AttnArgs {
   int max_splits;     // per (row, kv head)
   float* part_o;      // [M][NQ][max_splits][HD]
   float* part_ml;     // [M][NQ][max_splits][2]
-  unsigned int* arrive;  // [M][KVH], zero between uses
+  unsigned int* arrive;  // [2][m_rows][KVH] split arrivals then finishes, zero between uses
   int* err;
 };
 
@@ -550,7 +550,7 @@ constexpr int kAttnRound = 64;
 template <typename KT, int HD>
 constexpr int attn_smem_floats() {
   return (int)(2 * kAttnRound * HD * sizeof(KT) / sizeof(float)) + 2 * kWarps + kWarps * HD +
-         2 * kGMax * kAttnMaxSplits + kGMax;
+         2 * kGMax * kAttnMaxSplits + kGMax + 32 * 16;
 }
 
 // 16-byte asynchronous copy global -> shared (no register staging), cached in
@@ -642,63 +642,108 @@ DLLM_DEV void attn_finish(const AttnArgs& A, int m, int g, int s, int nsplit, in
     __syncthreads();
     return;
   }
-  // last CTA to finish this (row, g) merges the splits: one acq_rel ticket per CTA
-  // publishes this CTA's partials and, for the last one, acquires everyone's
+  // All nsplit CTAs of this (row, kv head) are resident (cooperative launch)
+  // and hold one split each (nsplit <= kAttnMaxSplits < grid), so they can wait
+  // for each other: each arrives with an acq_rel add (publishing its partials),
+  // waits (bounded) until every split has arrived, then merges a 1/nsplit share
+  // of the G*HD outputs. The last CTA to finish resets both counters.
   __syncthreads();
-  __shared__ int s_last;
+  unsigned int* arr = A.arrive + m * A.KVH + g;
+  unsigned int* fin = A.arrive + (A.m_rows + m) * A.KVH + g;
+  __shared__ int s_go;
   if (threadIdx.x == 0) {
-    const unsigned int t = atom_add_acq_rel_u32(&A.arrive[m * A.KVH + g], 1u);
-    s_last = (t == (unsigned int)nsplit - 1);
+    atom_add_acq_rel_u32(arr, 1u);
+    int ok = 1;
+    const long long t0 = clock64();
+    while (ld_acquire_u32(arr) < (unsigned int)nsplit) {
+      if (clock64() - t0 > kBarrierTimeoutCycles) {
+        atomicExch(A.err, kErrBarrier);
+        ok = 0;
+        break;
+      }
+    }
+    s_go = ok;
   }
   __syncthreads();
-  if (s_last) {
-    // split maxima and sums -> shared memory, one parallel pass
-    float* sm_m = mrg;                       // [G][nsplit]
-    float* sm_l = sm_m + kGMax * nsplit;     // [G][nsplit]; becomes the split weights
-    float* sm_den = sm_l + kGMax * nsplit;   // [G]
-    for (int i = threadIdx.x; i < G * nsplit; i += blockDim.x) {
+  if (!s_go) return;
+  const int nout = G * HD;
+  const int per = (nout + nsplit - 1) / nsplit;
+  const int o0 = s * per, o1 = min(nout, o0 + per);
+  if (o0 < o1) {
+    const int h0 = o0 / HD, h1 = (o1 - 1) / HD;  // heads this share touches
+    const int nh = h1 - h0 + 1;
+    float* sm_m = mrg;                        // [nh][nsplit]
+    float* sm_w = sm_m + kGMax * nsplit;      // [nh][nsplit] split weights
+    float* sm_den = sm_w + kGMax * nsplit;    // [nh]
+    float* sm_p = sm_den + kGMax;             // [32][16] partial sums
+    // one round of loads: the split maxima/sums of the heads, and up to 4 split
+    // outputs per thread (thread = output i of a block of 32 x split group sg)
+    for (int i = threadIdx.x; i < nh * nsplit; i += blockDim.x) {
       const int hh = i / nsplit, k = i - hh * nsplit;
-      const float* ml = A.part_ml + (((size_t)m * A.NQ + g * G + hh) * A.max_splits + k) * 2;
+      const float* ml = A.part_ml + (((size_t)m * A.NQ + g * G + h0 + hh) * A.max_splits + k) * 2;
       sm_m[i] = __ldcg(ml);
-      sm_l[i] = __ldcg(ml + 1);
+      sm_w[i] = __ldcg(ml + 1);
     }
-    __syncthreads();
-    // per head (one warp each): max over splits, split weights exp(m_s - max), denominator
-    for (int hh = warp; hh < G; hh += nwarps) {
-      float mx = -INFINITY;
-      for (int k = lane; k < nsplit; k += 32) mx = fmaxf(mx, sm_m[hh * nsplit + k]);
-      mx = warp_max(mx);
-      float den = 0.f;
-      for (int k = lane; k < nsplit; k += 32) {
-        const float f = expf(sm_m[hh * nsplit + k] - mx);
-        den = fmaf(sm_l[hh * nsplit + k], f, den);
-        sm_l[hh * nsplit + k] = f;
-      }
-      den = warp_sum(den);
-      if (lane == 0) sm_den[hh] = den;
-    }
-    __syncthreads();
-    // out[h][d] = sum_s w[h][s] * o_s[h][d] / den[h]; loads issued in batches of 8
-    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
-      const int hh = i / HD, d = i - hh * HD;
-      const float* po = A.part_o + ((size_t)m * A.NQ + g * G + hh) * A.max_splits * HD + d;
-      const float* wv = sm_l + hh * nsplit;
-      float o = 0.f;
-      for (int k0 = 0; k0 < nsplit; k0 += 8) {
-        float pvv[8];
+    const int sg = threadIdx.x & 15, oi = threadIdx.x >> 4;  // 16 split groups x 32 outputs
+    for (int ob = o0; ob < o1; ob += 32) {
+      const int o = ob + oi;
+      const bool has = o < o1;
+      float v[kAttnMaxSplits / 16];
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) pvv[kk] = (k0 + kk < nsplit) ? __ldcg(po + (size_t)(k0 + kk) * HD) : 0.f;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          if (k0 + kk < nsplit) o = fmaf(wv[k0 + kk], pvv[kk], o);
+      for (int r = 0; r < kAttnMaxSplits / 16; ++r) {
+        const int kk = sg + 16 * r;
+        v[r] = (has && kk < nsplit)
+                   ? __ldcg(A.part_o + (((size_t)m * A.NQ + g * G + o / HD) * A.max_splits + kk) * HD + (o % HD))
+                   : 0.f;
       }
-      out_row[hh * HD + d] = __fdiv_rn(o, sm_den[hh]);
+      __syncthreads();
+      if (ob == o0) {
+        // per head (one warp each): max over splits, weights exp(m_s - max), denominator
+        for (int hh = warp; hh < nh; hh += nwarps) {
+          float mx = -INFINITY;
+          for (int k = lane; k < nsplit; k += 32) mx = fmaxf(mx, sm_m[hh * nsplit + k]);
+          mx = warp_max(mx);
+          float den = 0.f;
+          for (int k = lane; k < nsplit; k += 32) {
+            const float f = expf(sm_m[hh * nsplit + k] - mx);
+            den = fmaf(sm_w[hh * nsplit + k], f, den);
+            sm_w[hh * nsplit + k] = f;
+          }
+          den = warp_sum(den);
+          if (lane == 0) sm_den[hh] = den;
+        }
+        __syncthreads();
+      }
+      float acc = 0.f;
+      if (has) {
+        const float* w = sm_w + (o / HD - h0) * nsplit;
+#pragma unroll
+        for (int r = 0; r < kAttnMaxSplits / 16; ++r) {
+          const int kk = sg + 16 * r;
+          if (kk < nsplit) acc = fmaf(w[kk], v[r], acc);
+        }
+      }
+      sm_p[oi * 16 + sg] = acc;
+      __syncthreads();
+      if (threadIdx.x < 32 && ob + (int)threadIdx.x < o1) {
+        const int oo = ob + threadIdx.x;
+        float tot = 0.f;
+        for (int q = 0; q < 16; ++q) tot += sm_p[threadIdx.x * 16 + q];  // fixed order
+        out_row[oo] = __fdiv_rn(tot, sm_den[oo / HD - h0]);
+      }
+      __syncthreads();
     }
-    if (threadIdx.x == 0) A.arrive[m * A.KVH + g] = 0u;
+  }
+  if (threadIdx.x == 0) {
+    // every CTA of the group passed its wait before arriving here
+    const unsigned int d = atom_add_acq_rel_u32(fin, 1u);
+    if (d == (unsigned int)nsplit - 1) {
+      *arr = 0u;
+      *fin = 0u;
+    }
   }
   __syncthreads();
 }
-
 
 // Attention for one work item (row m, kv head g, split s); called by the whole
 // CTA. The item's slots are taken in rounds of kAttnRound: all threads copy the

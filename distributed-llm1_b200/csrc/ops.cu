@@ -157,10 +157,21 @@ __global__ void __launch_bounds__(kThreads, 1) attention_op_kernel(const AttnArg
   attn_phase<float, HD>(A, smem, blockIdx.x, gridDim.x);
 }
 
+// Cooperative launch: the CTAs holding the splits of one (row, kv head) wait for
+// each other before merging, so all of them must be resident.
 template <int HD>
 static cudaError_t launch_attention(const AttnArgs& A, int sms, cudaStream_t st) {
-  attention_op_kernel<HD><<<sms, kThreads, attn_smem_bytes<HD>(), st>>>(A);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(sms);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = attn_smem_bytes<HD>();
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, attention_op_kernel<HD>, A);
 }
 
 cudaError_t configure_op_kernels() {
@@ -348,7 +359,7 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 
 __global__ void noalloc_attn_init(RowDesc* rows, unsigned int* arrive, int* err, int t0, int n, int kvh) {
   for (int i = threadIdx.x; i < n; i += blockDim.x) rows[i] = RowDesc{0, t0 + i, t0 + i, 0};
-  for (int i = threadIdx.x; i < n * kvh; i += blockDim.x) arrive[i] = 0u;
+  for (int i = threadIdx.x; i < 2 * n * kvh; i += blockDim.x) arrive[i] = 0u;  // arrivals, finishes
   if (threadIdx.x == 0) *err = 0;
 }
 
@@ -364,7 +375,7 @@ static NoAllocLayout noalloc_layout(int n, int nq, int kvh, int hd, int splits) 
   L.rows = off;
   off = align256(off + sizeof(RowDesc) * (size_t)n);
   L.arrive = off;
-  off = align256(off + sizeof(unsigned int) * (size_t)n * kvh);
+  off = align256(off + sizeof(unsigned int) * 2 * (size_t)n * kvh);
   L.err = off;
   off = align256(off + sizeof(int));
   L.part_ml = off;

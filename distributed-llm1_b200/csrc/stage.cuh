@@ -31,7 +31,7 @@ struct StageParams {
   float* mid;            // [M][I]
   float* part_o;         // attention split partials
   float* part_ml;
-  unsigned int* arrive;  // [M][KVH]
+  unsigned int* arrive;  // [2][M][KVH] attention split arrivals, finishes
   int max_splits;
   KvLayout kv;           // k/v bases unused (per layer in LayerW)
   // optional first phase: h[m] = embed[tokens_in[m]]
