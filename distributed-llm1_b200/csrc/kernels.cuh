@@ -175,19 +175,31 @@ struct PhaseSmem {
 };
 
 // ---- matvec phase ----------------------------------------------------------------
+// CTA `cta` of `ncta` owns units [u0, u1): equal contiguous ranges, or ranges
+// whose bounds are multiples of `align` (the split-K MLP needs 16-byte aligned
+// column slices of down_proj).
+DLLM_DEV void unit_range(int units, int cta, int ncta, int align, int& u0, int& u1) {
+  u0 = (int)(((long long)cta * units) / ncta);
+  u1 = (int)(((long long)(cta + 1) * units) / ncta);
+  if (align > 1) {
+    u0 = u0 / align * align;
+    u1 = cta + 1 == ncta ? units : u1 / align * align;
+  }
+}
+
 // Epi supplies: R (rows per unit), unit_rows(u, K, p[R]) and unit(u, m, a[R], st).
 // CTA `cta` of `ncta` owns units [cta*units/ncta, (cta+1)*units/ncta).
 template <class Epi, int M>
 DLLM_DEV void gemv_phase(const Epi& epi, const GemvIn& in, int units, const PhaseSmem& sm, int cta, int ncta,
-                         typename Epi::State& st) {
+                         typename Epi::State& st, int align = 1) {
   constexpr int R = Epi::R;
   constexpr int kU = Seg<R>::U;
   constexpr int kSegChunks = Seg<R>::Chunks;
   constexpr int kSegElems = Seg<R>::Elems;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int K = in.K, Kc = K >> 3;
-  const int u0 = (int)(((long long)cta * units) / ncta);
-  const int u1 = (int)(((long long)(cta + 1) * units) / ncta);
+  int u0, u1;
+  unit_range(units, cta, ncta, align, u0, u1);
   const int nu = u1 - u0;
   const int nseg = (Kc + kSegChunks - 1) / kSegChunks;
   int seg_per_blk = sm.xs_floats / (M * kSegElems);
@@ -337,6 +349,8 @@ struct EpiSiluGate {
   const __nv_bfloat16* wu;
   float* out;
   int N;
+  float* slice = nullptr;  // optional (one row): this CTA's values, slice[u - slice_base], in shared memory
+  int slice_base = 0;
   DLLM_DEV void unit_rows(int u, int K, const uint4** p) const {
     p[0] = reinterpret_cast<const uint4*>(wg + (size_t)u * K);
     p[1] = reinterpret_cast<const uint4*>(wu + (size_t)u * K);
@@ -344,7 +358,9 @@ struct EpiSiluGate {
   DLLM_DEV void unit(int u, int m, const float* a, State&) const {
     const float g = a[0];
     const float silu = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
-    out[(size_t)m * N + u] = __fmul_rn(silu, a[1]);
+    const float v = __fmul_rn(silu, a[1]);
+    out[(size_t)m * N + u] = v;
+    if (slice) slice[u - slice_base] = v;
   }
 };
 
@@ -450,6 +466,87 @@ struct EpiArgmax {
       if (i == m && k > st.key[i]) st.key[i] = k;
   }
 };
+
+// ---- split-K MLP down projection (one row) --------------------------------------------
+// 16 values in 16 lanes (lanes of one half-warp, xor offsets 8..1): afterwards
+// lane l (of its half) holds the sum of v[l] over the 16 lanes. Fixed order.
+DLLM_DEV float transpose_reduce16(float (&v)[16]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 8; o >= 1; o >>= 1) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < o; ++i) {
+      const float send = up ? v[i] : v[i + o];
+      const float keep = up ? v[i + o] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  return v[0];
+}
+
+// This CTA's share of down_proj for one row: out[j] = sum over t < S of
+// Wd[j][k0 + t] * slice[t], for every output j < D, where slice is the CTA's own
+// SiLU(gate)*up values for columns [k0, k0 + S) (still in shared memory). Half-warp
+// = 16 lanes x 8 columns of one row; each lane keeps 16 rows' 16-byte weight
+// vectors in flight; the 16 row sums are transpose-reduced. S <= 128, k0 and the
+// row length I multiples of 8.
+DLLM_DEV void down_partial(const __nv_bfloat16* wd, int D, int I, int k0, int S, const float* slice, float* out) {
+  constexpr int U = 16;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int cl = lane & 15, rsub = lane >> 4;
+  const bool act = cl * 8 < S;
+  float4 xa = make_float4(0.f, 0.f, 0.f, 0.f), xb = xa;
+  if (act) {
+    xa = *reinterpret_cast<const float4*>(slice + cl * 8);
+    xb = *reinterpret_cast<const float4*>(slice + cl * 8 + 4);
+  }
+  const __nv_bfloat16* wcol = wd + k0 + cl * 8;
+  for (int jb = 0; jb < D; jb += nwarps * 2 * U) {
+    const int j0 = jb + warp * 2 * U + rsub * U;  // this half-warp's 16 rows
+    uint4 w[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      w[u] = (act && j0 + u < D) ? ld_stream16(wcol + (size_t)(j0 + u) * I) : make_uint4(0u, 0u, 0u, 0u);
+    float acc[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) acc[u] = dot8(w[u], xa, xb, 0.f);
+    const float tot = transpose_reduce16(acc);  // lane cl: row j0 + cl
+    if (j0 + cl < D) out[j0 + cl] = tot;
+  }
+}
+
+// down_proj result and residual for this CTA's rows: h[j] += sum over CTAs c
+// of part[c][j] (16 threads per row, each over c = g, g + 16, ...; the 16 sums
+// then added in order). red: >= blockDim.x floats of shared memory.
+DLLM_DEV void residual_reduce(const float* part, int D, int nparts, int cta, int ncta, float* h, float* red) {
+  const int v0 = (int)(((long long)cta * D) / ncta), v1 = (int)(((long long)(cta + 1) * D) / ncta);
+  const int r = threadIdx.x >> 4, gq = threadIdx.x & 15;
+  const int rows_per = blockDim.x >> 4;
+  for (int rb = v0; rb < v1; rb += rows_per) {
+    const int j = rb + r;
+    float hv = 0.f;
+    if (gq == 0 && j < v1) hv = __ldcg(h + j);
+    float s = 0.f;
+    if (j < v1) {
+      for (int c0 = gq; c0 < nparts; c0 += 16 * 8) {
+        float v[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) v[q] = (c0 + 16 * q < nparts) ? __ldcg(part + (size_t)(c0 + 16 * q) * D + j) : 0.f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) s += v[q];
+      }
+    }
+    red[threadIdx.x] = s;
+    __syncthreads();
+    if (gq == 0 && j < v1) {
+      float tot = 0.f;
+      for (int q = 0; q < 16; ++q) tot += red[r * 16 + q];
+      h[j] = __fadd_rn(hv, tot);
+    }
+    __syncthreads();
+  }
+}
 
 // ---- decode attention phase (ATTENTION, kernels.js:86-132) ------------------------------
 // Row m's query attends to slots [0, slot_m] of its sequence. Work item =

@@ -15,8 +15,22 @@ cudaError_t configure_stage_kernels() {
   return e;
 }
 
-cudaError_t launch_stage(const StageParams& p, int kv_dtype, int grid, cudaStream_t st) {
-  if (p.m_rows < 1 || p.m_rows > 8) return cudaErrorInvalidValue;
+// The split-K MLP (one row) needs 8-aligned column slices of down_proj of at
+// most 128 columns per CTA (16 lanes x 8), and a partials buffer.
+static bool splitk_fits(const StageParams& p, int grid) {
+  if (p.m_rows != 1 || !p.dpart || p.I % 8 != 0 || grid < 1) return false;
+  for (int c = 0; c < grid; ++c) {
+    int u0 = (int)(((long long)c * p.I) / grid) / 8 * 8;
+    int u1 = c + 1 == grid ? p.I : (int)(((long long)(c + 1) * p.I) / grid) / 8 * 8;
+    if (u1 - u0 > 128) return false;
+  }
+  return true;
+}
+
+cudaError_t launch_stage(const StageParams& p0, int kv_dtype, int grid, cudaStream_t st) {
+  if (p0.m_rows < 1 || p0.m_rows > 8) return cudaErrorInvalidValue;
+  StageParams p = p0;
+  p.splitk = splitk_fits(p, grid) ? 1 : 0;
   // the grid barrier's counter starts every launch at zero (a memset node when
   // the launch is captured into a graph)
   cudaError_t e = cudaMemsetAsync(p.bar_count, 0, sizeof(unsigned int), st);

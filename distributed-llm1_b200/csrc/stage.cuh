@@ -54,6 +54,8 @@ struct StageParams {
   int pref_bytes;            // per-CTA L2 prefetch budget for the next phase
   unsigned long long* trace; // optional: %globaltimer (ns) at kernel start and after every barrier
   int trace_cap;
+  float* dpart;              // split-K MLP: [grid][D] down_proj partials (one row)
+  int splitk;                // use the split-K MLP (set by the host for one-row passes)
   int xs_floats;             // dynamic smem partition
   int part_floats;
 };

@@ -83,6 +83,35 @@ __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P)
     trace();
 
     // ---- rmsnorm -> gate, up -> siluMul (pipeline.js:69-72)
+    if (M == 1 && P.splitk) {
+      // Split-K MLP (one row): each CTA keeps its 8-aligned slice of SiLU(gate)*up
+      // in shared memory and multiplies it straight into its column slice of
+      // down_proj for all rows (no barrier, no staging of the whole vector);
+      // the per-CTA partials are then summed per output row with the residual.
+      int k0, k1;
+      unit_range(P.I, cta, ncta, 8, k0, k1);
+      float* slice = smem + P.xs_floats - 256;
+      EpiSiluGate eg{L.wg, L.wu, P.mid, P.I, slice, k0};
+      gemv_phase<EpiSiluGate, M>(eg, GemvIn{P.h, D, P.m_rows, L.ln2, P.eps}, P.I, sm, cta, ncta, ns, 8);
+      // ---- down_proj (pipeline.js:73), this CTA's K-slice
+      down_partial(L.wd, D, P.I, k0, k1 - k0, slice, P.dpart + (size_t)cta * D);
+      if (!grid_barrier(P.bar_count, P.err)) return;
+      trace();
+      // ---- + residual (pipeline.js:74): per-row sum of the partials
+      residual_reduce(P.dpart, D, ncta, cta, ncta, P.h, smem + P.xs_floats);
+      if (l + 1 < P.n_layers) {
+        const LayerW Ln = P.layers[l + 1];
+        const EpiQKV<KT> en{Ln.wq, Ln.wk, Ln.wv, nullptr, nullptr, nullptr, P.NQ, P.KVH, P.HD, P.log2_half};
+        prefetch_phase(en, D, qkv_units, cta, ncta, P.pref_bytes);
+      } else if (P.lm_head) {
+        const EpiArgmax<M> ep{P.lm_head, P.V, nullptr};
+        prefetch_phase(ep, D, P.V, cta, ncta, P.pref_bytes);
+      }
+      if (!grid_barrier(P.bar_count, P.err)) return;
+      trace();
+      continue;
+    }
+    // ---- rmsnorm -> gate, up -> siluMul (pipeline.js:69-72)
     gemv_phase<EpiSiluGate, M>(eg, GemvIn{P.h, D, P.m_rows, L.ln2, P.eps}, P.I, sm, cta, ncta, ns);
     const EpiResidual ed{L.wd, P.h, D};
     prefetch_phase(ed, P.I, D, cta, ncta, P.pref_bytes);
