@@ -3,9 +3,6 @@
 // Everything here is hand-written PTX for Blackwell (sm_100a) or plain CUDA C++:
 //   * streaming 16-byte weight loads that bypass L1 (weights are read exactly once
 //     per decode step, so they must not evict the activations L1 holds),
-//   * programmatic dependent launch (PDL) control: a kernel may start while its
-//     predecessor drains, warm L2 with its own weights, and only then wait for the
-//     predecessor's activations (griddepcontrol.wait),
 //   * the TMA engine's bulk L2 prefetch (cp.async.bulk.prefetch.L2),
 //   * bf16 <-> fp32 bit helpers matching weights.js:153-164 (value = bits << 16).
 #pragma once
@@ -18,14 +15,6 @@
 
 namespace dllm {
 
-// ---- programmatic dependent launch ------------------------------------------
-// Block until every grid this one depends on has completed and its memory is
-// visible. A no-op when the kernel was launched without the PDL attribute.
-DLLM_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-// Let the next kernel in the stream begin launching (its CTAs still wait for
-// this grid's completion before touching data this grid writes).
-DLLM_DEV void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-
 // ---- memory -------------------------------------------------------------------
 // 16-byte streaming load of read-only data: no L1 allocation, 256-byte L2 fetch.
 DLLM_DEV uint4 ld_stream16(const void* p) {
@@ -33,13 +22,6 @@ DLLM_DEV uint4 ld_stream16(const void* p) {
   asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                : "l"(p));
-  return r;
-}
-
-// 8-byte streaming load.
-DLLM_DEV uint2 ld_stream8(const void* p) {
-  uint2 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
   return r;
 }
 
@@ -55,9 +37,6 @@ DLLM_DEV unsigned long long global_timer_ns() {
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
-
-// L2-coherent loads for data produced by other CTAs of the same grid.
-DLLM_DEV float ld_cg(const float* p) { return __ldcg(p); }
 
 // ---- bf16 bit helpers (weights.js:153-164: f32 bits = bf16 bits << 16) --------
 DLLM_DEV float bf16_lo(uint32_t u) { return __uint_as_float(u << 16); }
@@ -103,11 +82,6 @@ DLLM_DEV unsigned long long argmax_key(float v, int idx) {
   return ((unsigned long long)ord << 32) | (unsigned long long)(~(uint32_t)idx);
 }
 DLLM_DEV int argmax_key_index(unsigned long long key) { return (int)(~(uint32_t)(key & 0xffffffffull)); }
-DLLM_DEV float argmax_key_value(unsigned long long key) {
-  uint32_t ord = (uint32_t)(key >> 32);
-  uint32_t u = (ord & 0x80000000u) ? (ord & 0x7fffffffu) : ~ord;
-  return __uint_as_float(u);
-}
 
 // ---- per-row decode descriptor ----------------------------------------------------
 // One row of a forward: which sequence it belongs to, the RoPE position, and

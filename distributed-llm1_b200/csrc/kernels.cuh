@@ -36,7 +36,6 @@ struct Seg {
   static constexpr int Chunks = 32 * U;  // 16-byte chunks per task segment
   static constexpr int Elems = Chunks * 8;
 };
-constexpr int kSegElemsMax = Seg<1>::Elems;
 constexpr int kGMax = 8;                 // max query heads per KV head
 constexpr int kAttnMaxSplits = 64;       // max attention splits per (row, kv head)
 constexpr int kMaxRows = 8;              // max rows (sequences or prompt tokens) per pass
@@ -586,58 +585,6 @@ DLLM_DEV int attn_splits(int T, int max_splits, int nsub, int* chunk_out) {
   return ns;
 }
 
-// 16-byte KV vector: 4 fp32 or 8 bf16 elements (slot row of the q.k pass).
-template <typename KT>
-struct KvVec16;
-template <>
-struct KvVec16<float> {
-  static constexpr int N = 4;
-  DLLM_DEV static void unpack(uint4 t, float (&v)[4]) {
-    v[0] = __uint_as_float(t.x); v[1] = __uint_as_float(t.y); v[2] = __uint_as_float(t.z); v[3] = __uint_as_float(t.w);
-  }
-  DLLM_DEV static void load(const float* p, float (&v)[4]) {
-    const float4 t = __ldcg(reinterpret_cast<const float4*>(p));
-    v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
-  }
-};
-template <>
-struct KvVec16<__nv_bfloat16> {
-  static constexpr int N = 8;
-  DLLM_DEV static void unpack(uint4 t, float (&v)[8]) {
-    v[0] = bf16_lo(t.x); v[1] = bf16_hi(t.x); v[2] = bf16_lo(t.y); v[3] = bf16_hi(t.y);
-    v[4] = bf16_lo(t.z); v[5] = bf16_hi(t.z); v[6] = bf16_lo(t.w); v[7] = bf16_hi(t.w);
-  }
-  DLLM_DEV static void load(const __nv_bfloat16* p, float (&v)[8]) {
-    const uint4 t = __ldcg(reinterpret_cast<const uint4*>(p));
-    v[0] = bf16_lo(t.x); v[1] = bf16_hi(t.x); v[2] = bf16_lo(t.y); v[3] = bf16_hi(t.y);
-    v[4] = bf16_lo(t.z); v[5] = bf16_hi(t.z); v[6] = bf16_lo(t.w); v[7] = bf16_hi(t.w);
-  }
-};
-
-template <typename KT>
-DLLM_DEV void load_vec4(const KT* p, float (&v)[4]);
-template <>
-DLLM_DEV void load_vec4<float>(const float* p, float (&v)[4]) {
-  const float4 t = __ldcg(reinterpret_cast<const float4*>(p));
-  v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
-}
-template <>
-DLLM_DEV void load_vec4<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[4]) {
-  const uint2 t = __ldcg(reinterpret_cast<const uint2*>(p));
-  v[0] = bf16_lo(t.x); v[1] = bf16_hi(t.x); v[2] = bf16_lo(t.y); v[3] = bf16_hi(t.y);
-}
-template <typename KT>
-DLLM_DEV void load_vec2(const KT* p, float (&v)[2]);
-template <>
-DLLM_DEV void load_vec2<float>(const float* p, float (&v)[2]) {
-  const float2 t = __ldcg(reinterpret_cast<const float2*>(p));
-  v[0] = t.x; v[1] = t.y;
-}
-template <>
-DLLM_DEV void load_vec2<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[2]) {
-  const uint32_t t = __ldcg(reinterpret_cast<const unsigned int*>(p));
-  v[0] = bf16_lo(t); v[1] = bf16_hi(t);
-}
 
 // Slots of one K/V staging round of an attention item (a multiple of 32).
 constexpr int kAttnRound = 64;
