@@ -11,7 +11,7 @@ from . import _lib, constants, frames, weights
 from .constants import CFG, FRAME, PRESETS, ModelConfig
 from .kernels import GpuBuffer, KernelContext, initKernels, init_kernels
 from .pipeline import LeaderPipeline, LocalTransport, Stage, assignLayers, assign_layers, handle_stage_frame, plan_stages
-from .weights import bf16BitsToF32, bf16BytesToF32Bits, reinterpretBits, tensorsForLayers
+from .weights import bf16BitsToF32, bf16BytesToF32Bits, load_checkpoint, reinterpretBits, tensorsForLayers
 from ._lib import DllmError, KvOverflowError
 
 LIB_PATH = _lib.LIB_PATH

@@ -110,3 +110,60 @@ def write_safetensors(path: str, tensors: dict[str, np.ndarray], shapes: dict[st
         for a in blobs:
             f.write(a.tobytes())
     os.replace(tmp, path)
+
+
+# ---- checkpoint slices straight to the device ----------------------------------------------
+def checkpoint_files(path: str) -> list[str]:
+    """The safetensors files of a checkpoint: `path` itself, the shards named by a
+    Hugging Face `model.safetensors.index.json` (given directly or inside the
+    directory `path`), or every `*.safetensors` file of the directory."""
+    if os.path.isdir(path):
+        idx = os.path.join(path, "model.safetensors.index.json")
+        if os.path.exists(idx):
+            path = idx
+        else:
+            files = sorted(os.path.join(path, f) for f in os.listdir(path) if f.endswith(".safetensors"))
+            if not files:
+                raise FileNotFoundError(f"no .safetensors files in {path}")
+            return files
+    if path.endswith(".json"):
+        with open(path) as f:
+            wm = json.load(f)["weight_map"]
+        base = os.path.dirname(path)
+        return sorted({os.path.join(base, v) for v in wm.values()})
+    return [path]
+
+
+def load_checkpoint(kctx, path: str, start: int, end: int, stage=None, leader=None) -> list[str]:
+    """Upload the tensors a stage owning layers [start, end) needs (tensorsForLayers,
+    weights.js:167-182), one tensor at a time from the memory-mapped file to the
+    device, so the host holds one tensor at most. `stage` receives the layer
+    tensors (`stage.W[name]`); `leader` (a LeaderPipeline) the embedding, final
+    norm and, for untied models, `lm_head.weight`. Returns the names uploaded;
+    names the checkpoint lacks (e.g. biases of a bias-free model) are skipped."""
+    where = {}
+    maps = {}
+    for f in checkpoint_files(path):
+        maps[f] = read_tensor_map(f)
+        for n in maps[f]:
+            where.setdefault(n, f)
+    done = []
+
+    def one(name):
+        f = where.get(name)
+        if f is None:
+            return None
+        bits = read_tensors(f, [name], maps[f])[name]
+        buf = kctx.loadWeightBf16(bits, name)
+        done.append(name)
+        return buf
+
+    if stage is not None:
+        for name in tensorsForLayers(start, end, False):
+            buf = one(name)
+            if buf is not None:
+                stage.W[name] = buf
+    if leader is not None:
+        embed, norm, head = one("model.embed_tokens.weight"), one("model.norm.weight"), one("lm_head.weight")
+        leader.setLeaderWeights(embed, norm, head)
+    return done
