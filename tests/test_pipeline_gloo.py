@@ -101,3 +101,50 @@ def test_plan_fill_and_steady_state():
             nxt = (r + 1) % world
             for tick in range(4 * world):
                 assert mg.Plan(r, world, world, 1).send_at(tick) == mg.Plan(nxt, world, world, 1).recv_at(tick)
+
+
+def failing_worker(rank, world, port, path):
+    """Rank 1's stage fails at tick 3 and the rank leaves; rank 0 records how its
+    own run ended and how long that took."""
+    import datetime
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    mg = importlib.import_module("distributed-llm1_b200.multigpu")
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    plan = mg.Plan(rank, world, world, 1)
+    first = torch.arange(world, dtype=torch.int32) + 1
+    runner = None
+
+    def compute(b, h, ti, to):
+        if rank == 1 and runner.tick >= 3:
+            raise RuntimeError("stage 1 failed")
+        stage_fn(rank, world, h, ti, to)
+
+    runner = mg.PipelineRunner(plan, D, "cpu", compute, first)
+    t0 = time.time()
+    try:
+        runner.run_ticks(40)
+        outcome = "completed"
+    except Exception as e:  # the failure, or the peer's disappearance
+        outcome = type(e).__name__
+    if rank == 0:
+        with open(path, "w") as f:
+            f.write(f"{outcome} {time.time() - t0:.2f} {runner.tick}")
+    os._exit(0)  # the peer is gone: no collective teardown
+
+
+def test_stage_failure_surfaces_on_other_ranks():
+    """A rank whose stage raises leaves between ticks; the other rank's next
+    exchange ends with an error within the process-group timeout instead of
+    hanging (failure detection on the host, no GPU involved)."""
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    if root not in sys.path:
+        sys.path.insert(0, root)
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "outcome.txt")
+        mp.start_processes(failing_worker, args=(2, free_port(), path), nprocs=2, start_method="spawn", join=True)
+        outcome, secs, tick = open(path).read().split()
+    assert outcome != "completed"
+    assert float(secs) < 30.0
+    assert 3 <= int(tick) < 40
