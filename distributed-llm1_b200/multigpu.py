@@ -186,6 +186,14 @@ def bench_pipeline(args, bench):
     tick_s = ms / 1000.0 / (args.steps * B)
     peak, peak_kind = bench.measured_peaks()
     achieved = max(stage_bytes) / tick_s / 1e9
+    # DRAM traffic of the slowest stage's launch: the committed ncu traffic /
+    # algorithmic ratio of the whole-model token applied to the stage's bytes
+    full_traffic = bench.traffic_from_profile()
+    traffic = None
+    if full_traffic is not None and args.model == "qwen2.5-7b":
+        full_alg = bench.token_bytes(cfg.with_(kv_dtype="bf16"), cfg.num_layers, head=True, embed=True,
+                                     kv_positions=args.kv_len + args.warmup + args.steps / 2)
+        traffic = max(stage_bytes) * full_traffic / full_alg
     # e2e: the same loop with every tick's tokens copied to the host and checked
     e2e = None
     res = None
@@ -196,7 +204,7 @@ def bench_pipeline(args, bench):
                "data": "synthetic: random-init N(0,0.02) bf16 weights (device hash), N(0,1) bf16 KV",
                "config": bench.workload_config(args, cfg) | {"stages": dllm.plan_stages(cfg, world)},
                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                            "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
+                            "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
                             "algorithmic_bytes_per_launch": max(stage_bytes),
                             "kernel": "stage_kernel of the slowest stage (one launch per micro-batch tick)"},
                "gpu_launches": launches, "clocks": clk.summary()}
