@@ -63,6 +63,7 @@ struct StageParams {
 // Dynamic shared memory the stage kernel is launched with.
 constexpr int kStageXsFloats = 32768;    // 128 KB of staged activations
 constexpr int kStagePartFloats = 16384;  // 64 KB of segment partials
+constexpr int kStageSmallPartFloats = 4096;  // 16 KB: the one-row split-K partition
 constexpr size_t kStageSmemBytes = (size_t)(kStageXsFloats + kStagePartFloats) * sizeof(float);
 
 // Launches stage_kernel<KT, HD, M> with M the smallest of {1,2,4,8} >= m_rows,

@@ -92,7 +92,8 @@ __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P)
       unit_range(P.I, cta, ncta, 8, k0, k1);
       float* slice = smem + P.xs_floats - 256;
       EpiSiluGate eg{L.wg, L.wu, P.mid, P.I, slice, k0};
-      gemv_phase<EpiSiluGate, M>(eg, GemvIn{P.h, D, P.m_rows, L.ln2, P.eps}, P.I, sm, cta, ncta, ns, 8);
+      const PhaseSmem sm_g{smem, P.xs_floats - 256, sm.part, sm.part_floats, red};  // staging stops short of the slice
+      gemv_phase<EpiSiluGate, M>(eg, GemvIn{P.h, D, P.m_rows, L.ln2, P.eps}, P.I, sm_g, cta, ncta, ns, 8);
       // ---- down_proj (pipeline.js:73), this CTA's K-slice
       down_partial(L.wd, D, P.I, k0, k1 - k0, slice, P.dpart + (size_t)cta * D);
       if (!grid_barrier(P.bar_count, P.err)) return;
@@ -178,12 +179,28 @@ __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P)
 }
 
 template <typename KT, int HD, int M>
-static cudaError_t launch_one(const StageParams& p, int grid, cudaStream_t st) {
+static cudaError_t launch_one(const StageParams& p0, int grid, cudaStream_t st) {
   auto fn = stage_kernel<KT, HD, M>;
+  StageParams p = p0;
+  if (M == 1 && p.splitk) {
+    // One row with the split-K MLP: no phase stages more than a D- or
+    // NQ*HD-long activation (mid is never staged), so a small shared-memory
+    // partition suffices and the rest of the SM's 256 KB stays L1, which the
+    // in-flight weight loads need.
+    const int K = p.D > p.NQ * p.HD ? p.D : p.NQ * p.HD;
+    int xs = ((K + 4095) / 4096) * 4096 + 256;  // staged x + the SiLU(gate)*up slice
+    const int part = kStageSmallPartFloats;
+    if (xs + part < attn_smem_floats<KT, HD>()) xs = attn_smem_floats<KT, HD>() - part;
+    xs = (xs + 3) & ~3;  // 16-byte aligned partial and slice areas
+    if (xs + part < kStageXsFloats + kStagePartFloats) {
+      p.xs_floats = xs;
+      p.part_floats = part;
+    }
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = kStageSmemBytes;
+  cfg.dynamicSmemBytes = (size_t)(p.xs_floats + p.part_floats) * sizeof(float);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;
