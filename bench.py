@@ -19,7 +19,8 @@ and KV exceed L2 (126 MB), so no L2 flush is needed between steps.
 `--impl reference` times the reference's CPU path: the reference is JavaScript +
 WebGPU with no runtime on this machine, so its loops are timed through the C++
 restatement (oracle/ref_forward.cpp, reference loop order) on all host cores,
-on a bounded sample of layers scaled to a full token.
+every step one full token (all layers, final norm, LM head), timed, not
+extrapolated.
 """
 from __future__ import annotations
 
@@ -51,7 +52,6 @@ def parse_args():
     p.add_argument("--kv-len", type=int, default=KV_LEN)
     p.add_argument("--micro", type=int, default=1, help="sequences per micro-batch (N>1)")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--cpu-layers", type=int, default=2, help="layers in the CPU baseline sample")
     p.add_argument("--cpu-steps", type=int, default=3, help="tokens in the CPU baseline sample")
     p.add_argument("--layers", type=int, default=0,
                    help="profiling case only: run the first N layers + LM head (a few GB on the device); "
@@ -67,17 +67,17 @@ def measured_peaks() -> tuple[float, str]:
         return 6650.0, "fallback"
 
 
-def traffic_from_profile() -> float | None:
-    """DRAM bytes per stage-kernel launch from the committed ncu summary, if any
-    (line `dram_bytes_per_token_7b: <bytes>`)."""
-    path = os.path.join(ROOT, "profiles", "stage_kernel_qwen7b_decode.md")
-    try:
-        for line in open(path):
-            if line.strip().startswith("dram_bytes_per_token_7b:"):
-                return float(line.split(":", 1)[1].strip())
-    except OSError:
-        pass
-    return None
+# DRAM traffic of the stage kernel per token, as a multiple of its algorithmic
+# bytes: dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture of the
+# 7B decode launch (2 layers + LM head, 2048-slot bf16 KV) over that launch's
+# weight + KV + embedding bytes. Re-measure with the profiling command when the
+# kernel changes.
+STAGE_TRAFFIC_RATIO = 1.0022
+
+
+def traffic_bytes(algorithmic: float, model: str) -> float | None:
+    """ncu-measured DRAM bytes per launch, scaled from the profiled 7B capture."""
+    return algorithmic * STAGE_TRAFFIC_RATIO if model == "qwen2.5-7b" else None
 
 
 # ---- clocks --------------------------------------------------------------------------
@@ -140,38 +140,8 @@ class ClockSampler:
 # ---- model setup on the device ------------------------------------------------------
 def device_weights(ctx, stage, cfg, start: int, end: int, embed: bool, head: bool, seed: int = 0):
     """Synthetic bf16 weights generated on the device: N(0, 0.02), norms 1.0."""
-    D, QD, KD, I, V = (cfg.hidden_size, cfg.num_q_heads * cfg.head_dim, cfg.num_kv_heads * cfg.head_dim,
-                       cfg.intermediate_size, cfg.vocab_size)
-    sizes = {"input_layernorm.weight": D, "post_attention_layernorm.weight": D,
-             "self_attn.q_proj.weight": QD * D, "self_attn.k_proj.weight": KD * D,
-             "self_attn.v_proj.weight": KD * D, "self_attn.o_proj.weight": D * QD,
-             "self_attn.q_proj.bias": QD, "self_attn.k_proj.bias": KD, "self_attn.v_proj.bias": KD,
-             "mlp.gate_proj.weight": I * D, "mlp.up_proj.weight": I * D, "mlp.down_proj.weight": D * I}
-    k = 0
-    for L in range(start, end):
-        for suf, n in sizes.items():
-            name = f"model.layers.{L}.{suf}"
-            b = ctx.createBf16(n, name)
-            if "layernorm" in suf:
-                ctx.fillConstBf16(b, 1.0)
-            else:
-                ctx.fillNormalBf16(b, seed * 100003 + L * 97 + k, WEIGHT_STD)
-            k += 1
-            stage.W[name] = b
-    bufs = {}
-    if embed or (head and cfg.tie_word_embeddings):
-        bufs["embed"] = ctx.createBf16(V * D, "model.embed_tokens.weight")
-        ctx.fillNormalBf16(bufs["embed"], seed * 100003 + 90001, WEIGHT_STD)
-        stage.W["model.embed_tokens.weight"] = bufs["embed"]
-    if head:
-        bufs["norm"] = ctx.createBf16(D, "model.norm.weight")
-        ctx.fillConstBf16(bufs["norm"], 1.0)
-        stage.W["model.norm.weight"] = bufs["norm"]
-        if not cfg.tie_word_embeddings:
-            bufs["lm_head"] = ctx.createBf16(V * D, "lm_head.weight")
-            ctx.fillNormalBf16(bufs["lm_head"], seed * 100003 + 90002, WEIGHT_STD)
-            stage.W["lm_head.weight"] = bufs["lm_head"]
-    return bufs
+    syn = importlib.import_module("distributed-llm1_b200.synthetic")
+    return syn.device_weights(ctx, stage, cfg, start, end, embed, head, seed)
 
 
 def token_bytes(cfg, layers: int, head: bool, embed: bool, kv_positions: float) -> float:
@@ -236,33 +206,33 @@ def _cpu_model(cfg, layers: int, kv_len: int, max_steps: int):
     return lib, m, keep, cores
 
 
-def cpu_token_times(cfg, layers: int, warmup: int, steps: int, kv_len: int):
-    """Per-token seconds of the reference loops for a full model, measured on a
-    sample of `layers` layers (scaled by num_layers / layers) plus the LM head."""
+def cpu_token_times(cfg, warmup: int, steps: int, kv_len: int):
+    """Per-token seconds of the reference loops through the whole model (every
+    layer, final norm, LM head) on all host cores, one decode token per step."""
     import numpy as np
-    lib, m, keep, cores = _cpu_model(cfg, layers, kv_len, warmup + steps)
+    lib, m, keep, cores = _cpu_model(cfg, cfg.num_layers, kv_len, warmup + steps)
     h = np.random.default_rng(0).standard_normal(cfg.hidden_size).astype(np.float32) * np.float32(0.05)
     times = []
     for s in range(warmup + steps):
         x = h.copy()
         t0 = time.perf_counter()
         lib.ref_stage_forward(m, x.ctypes.data, 1, kv_len + s)
-        t1 = time.perf_counter()
         lib.ref_sample_last(m, x.ctypes.data, None)
-        t2 = time.perf_counter()
+        t1 = time.perf_counter()
         if s >= warmup:
-            times.append((t1 - t0) * (cfg.num_layers / layers) + (t2 - t1))
+            times.append(t1 - t0)
     lib.ref_model_destroy(m)
+    del keep
     return times, cores
 
 
-def cpu_baseline(cfg, layers: int, steps: int, kv_len: int) -> dict:
-    times, cores = cpu_token_times(cfg, layers, 1, steps, kv_len)
+def cpu_baseline(cfg, steps: int, kv_len: int) -> dict:
+    times, cores = cpu_token_times(cfg, 1, steps, kv_len)
     per_token = sum(times) / len(times)
     return {"value": 1.0 / per_token, "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": (f"{steps} decode tokens (+1 warm-up) through {layers} of {cfg.num_layers} layers + final "
-                       f"norm + LM head at {kv_len}-slot KV on {cores} host threads, layer time scaled "
-                       f"x{cfg.num_layers / layers:g}; oracle/ref_forward.cpp (reference loop order, fp32)")}
+            "sample": (f"{steps} decode tokens (+1 warm-up) through all {cfg.num_layers} layers + final norm + "
+                       f"LM head at {kv_len}-slot KV on {cores} host threads; oracle/ref_forward.cpp "
+                       f"(reference loop order, fp32 arithmetic, bf16 weights and KV)")}
 
 
 def run_reference(args):
@@ -271,22 +241,20 @@ def run_reference(args):
     if rank != 0:
         return None
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import dataclasses
-
     import synth
     key = {"qwen2.5-0.5b": "0.5b", "qwen2.5-1.5b": "1.5b", "qwen2.5-7b": "7b", "qwen2.5-32b": "32b"}[args.model]
     cfg = synth.CONFIGS[key]
     cfg.kv_dtype = "bf16"
-    times, cores = cpu_token_times(cfg, args.cpu_layers, args.warmup, args.steps, args.kv_len)
+    times, cores = cpu_token_times(cfg, args.warmup, args.steps, args.kv_len)
     v = len(times) / sum(times)
     res = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True,
            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
            "config": workload_config(args, cfg),
            "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
-                            "sample": (f"each step: one decode token through {args.cpu_layers} of {cfg.num_layers} "
-                                       f"layers + final norm + LM head at {args.kv_len}-slot KV, layer time scaled "
-                                       f"x{cfg.num_layers / args.cpu_layers:g}; oracle/ref_forward.cpp")},
+                            "sample": (f"each step: one decode token through all {cfg.num_layers} layers + final "
+                                       f"norm + LM head at {args.kv_len}-slot KV (timed, not extrapolated); "
+                                       f"oracle/ref_forward.cpp")},
            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
            "note": "the reference is JavaScript + WebGPU with no JS engine or WebGPU adapter on this machine; "
                    "its loops are timed through the C++ restatement"}
@@ -341,7 +309,7 @@ def run_single(args):
     bytes_tok = token_bytes(cfg, cfg.num_layers, head=True, embed=True, kv_positions=avg_pos)
     peak, peak_kind = measured_peaks()
     achieved = bytes_tok / (ms / 1000.0 / args.steps) / 1e9
-    traffic = traffic_from_profile()
+    traffic = traffic_bytes(bytes_tok, args.model)
     # e2e: public generate call, token in from / out to host every step
     e2e_steps = args.steps
     gen_out = []
@@ -364,7 +332,7 @@ def run_single(args):
            "gpu_launches": launches, "clocks": clk.summary()}
     if not args.no_cpu_baseline:
         try:
-            res["cpu_baseline"] = cpu_baseline(cfg, args.cpu_layers, args.cpu_steps, args.kv_len)
+            res["cpu_baseline"] = cpu_baseline(cfg, args.cpu_steps, args.kv_len)
         except Exception as e:  # reported, never silently replaced
             res["cpu_baseline"] = {"value": None, "error": repr(e)}
     del bufs

@@ -96,6 +96,7 @@ SIGNATURES = {
     "dllm_stage_fill_kv_random": (C.c_int, [P, C.c_int, C.c_int, C.c_uint64]),
     "dllm_stage_set_page_table": (C.c_int, [P, C.c_int, I32P, C.c_int]),
     "dllm_stage_pages_per_seq": (C.c_int, [P]),
+    "dllm_stage_read_workspace": (C.c_int, [P, C.c_int, C.c_int, F32P]),
     "dllm_stage_set_trace": (C.c_int, [P, C.c_int]),
     "dllm_stage_read_trace": (C.c_int, [P, C.POINTER(C.c_uint64), C.c_int]),
     "dllm_leader_create": (C.c_int, [P, C.c_int, C.c_int, PP]),
@@ -113,6 +114,7 @@ SIGNATURES = {
     "dllm_leader_last_logits": (C.c_int, [P, F32P]),
     "dllm_leader_read_logits": (C.c_int, [P, C.c_int, F32P]),
     "dllm_attention_noalloc": (C.c_int, [P, P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, P]),
+    "dllm_attention_noalloc_status": (C.c_int, [P, C.c_int, I32P]),
 }
 
 _lib = None

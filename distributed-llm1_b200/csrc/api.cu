@@ -1218,6 +1218,25 @@ int dllm_stage_set_page_table(dllm_stage* s, int seq, const int32_t* pages, int 
 
 int dllm_stage_pages_per_seq(const dllm_stage* s) { return s ? s->pages_per_seq : -1; }
 
+int dllm_stage_read_workspace(dllm_stage* s, int which, int rows, float* dst) {
+  if (!s) return DLLM_EINVAL;
+  dllm_ctx* c = s->ctx;
+  const dllm_config& f = c->cfg;
+  if (!dst || rows < 1 || rows > dllm::kMaxRows)
+    return set_err(c, DLLM_EINVAL, "read_workspace: need 1..%d rows", dllm::kMaxRows);
+  const float* src = nullptr;
+  size_t width = 0;
+  switch (which) {
+    case 0: src = s->q; width = (size_t)f.num_q_heads * f.head_dim; break;
+    case 1: src = s->att; width = (size_t)f.num_q_heads * f.head_dim; break;
+    case 2: src = s->mid; width = (size_t)f.intermediate_size; break;
+    default: return set_err(c, DLLM_EINVAL, "read_workspace: which must be 0 (q), 1 (attention) or 2 (mlp)");
+  }
+  if (int rc = use_device(c)) return rc;
+  CK(c, cudaMemcpyAsync(dst, src, (size_t)rows * width * 4, cudaMemcpyDeviceToHost, c->stream));
+  return sync_check(c, kDefaultTimeoutMs);
+}
+
 int dllm_stage_set_trace(dllm_stage* s, int cap) {
   if (!s) return DLLM_EINVAL;
   dllm_ctx* c = s->ctx;

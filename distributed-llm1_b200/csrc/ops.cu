@@ -1,8 +1,9 @@
 // ops.cu — op-level kernels behind the ctx API of kernels.js (one launcher per
 // shader) and utility kernels (synthetic weights, KV cache access, argmax).
 // The matvec and attention ops reuse the phase code of the stage kernel.
+#include <chrono>
 #include <cmath>
-#include <mutex>
+#include <thread>
 
 #include "dllm.h"
 #include "kernels.cuh"
@@ -348,12 +349,12 @@ cudaError_t op_kv_write(const KvLayout& kv, void* pool, int kv_dtype, int seq, i
 // ---- attention without allocation -------------------------------------------------------
 // Scratch of dllm_attention_noalloc: every GPU that loads this library keeps these
 // bytes until the process exits. Calls share it, so calls that overlap on the GPU
-// race; the ticket counters are cleared by each call before its attention kernel.
+// race; each call's first kernel clears the error word and the ticket counters
+// before its attention kernel runs.
 namespace dllm {
 
 constexpr size_t kNoAllocScratchBytes = 4u << 20;  // 4 MiB
 constexpr int kNoAllocMaxRows = 64;
-constexpr int kNoAllocMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
@@ -365,19 +366,21 @@ __global__ void noalloc_attn_init(RowDesc* rows, unsigned int* arrive, int* err,
 
 static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 
-// Byte layout of the scratch for n rows and `splits` attention splits.
+// Byte layout of the scratch for n rows and `splits` attention splits. The error
+// word sits at offset 0 whatever the shape, so dllm_attention_noalloc_status can
+// read it without knowing the last call's arguments.
 struct NoAllocLayout {
-  size_t rows, arrive, err, part_ml, part_o, total;
+  size_t err, rows, arrive, part_ml, part_o, total;
 };
 static NoAllocLayout noalloc_layout(int n, int nq, int kvh, int hd, int splits) {
   NoAllocLayout L;
   size_t off = 0;
+  L.err = off;
+  off = align256(off + sizeof(int));
   L.rows = off;
   off = align256(off + sizeof(RowDesc) * (size_t)n);
   L.arrive = off;
   off = align256(off + sizeof(unsigned int) * 2 * (size_t)n * kvh);
-  L.err = off;
-  off = align256(off + sizeof(int));
   L.part_ml = off;
   off = align256(off + sizeof(float) * 2 * (size_t)n * nq * splits);
   L.part_o = off;
@@ -385,14 +388,6 @@ static NoAllocLayout noalloc_layout(int n, int nq, int kvh, int hd, int splits) 
   L.total = off;
   return L;
 }
-
-struct NoAllocDevice {
-  bool ready = false;
-  unsigned char* scratch = nullptr;  // device address of g_noalloc_scratch
-  int sms = 0;
-};
-static NoAllocDevice g_noalloc_dev[kNoAllocMaxDevices];
-static std::mutex g_noalloc_mu;
 
 }  // namespace dllm
 
@@ -406,42 +401,59 @@ extern "C" int dllm_attention_noalloc(const float* q, const float* kcache, const
   if (num_kv_heads < 1 || num_q_heads < 1 || num_q_heads % num_kv_heads || num_q_heads / num_kv_heads > kGMax)
     return DLLM_EINVAL;
   if (n > kNoAllocMaxRows) return DLLM_ERANGE;
+  // Every call, with the caller's device current: the device address of the static
+  // scratch in this context, the SM count, and the attention kernel's shared-memory
+  // limit. None of these allocates, and nothing is cached between calls, so the
+  // entry point stays valid across a device reset or a change of context.
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return DLLM_ECUDA;
-  NoAllocDevice& D = g_noalloc_dev[dev];
-  {
-    // once per device, with that device current: resolve the device address of the
-    // static scratch and raise the attention kernel's shared-memory limit
-    std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (!D.ready) {
-      void* p = nullptr;
-      if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return DLLM_ECUDA;
-      int sms = 0;
-      if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
-        return DLLM_ECUDA;
-      if (configure_op_kernels() != cudaSuccess) return DLLM_ECUDA;
-      D.scratch = static_cast<unsigned char*>(p);
-      D.sms = sms;
-      D.ready = true;
-    }
-  }
-  int splits = D.sms / ((n < 8 ? n : 8) * num_kv_heads);
+  if (cudaGetDevice(&dev) != cudaSuccess) return DLLM_ECUDA;
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return DLLM_ECUDA;
+  unsigned char* scratch = static_cast<unsigned char*>(p);
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1) return DLLM_ECUDA;
+  if (configure_op_kernels() != cudaSuccess) return DLLM_ECUDA;
+  int splits = sms / ((n < 8 ? n : 8) * num_kv_heads);
   if (splits > 64) splits = 64;
   if (splits < 1) splits = 1;
   NoAllocLayout L = noalloc_layout(n, num_q_heads, num_kv_heads, head_dim, splits);
   while (L.total > kNoAllocScratchBytes && splits > 1) L = noalloc_layout(n, num_q_heads, num_kv_heads, head_dim, --splits);
   if (L.total > kNoAllocScratchBytes) return DLLM_ERANGE;
   cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
-  RowDesc* rows = reinterpret_cast<RowDesc*>(D.scratch + L.rows);
-  unsigned int* arrive = reinterpret_cast<unsigned int*>(D.scratch + L.arrive);
-  int* err = reinterpret_cast<int*>(D.scratch + L.err);
+  RowDesc* rows = reinterpret_cast<RowDesc*>(scratch + L.rows);
+  unsigned int* arrive = reinterpret_cast<unsigned int*>(scratch + L.arrive);
+  int* err = reinterpret_cast<int*>(scratch + L.err);
   noalloc_attn_init<<<1, 256, 0, st>>>(rows, arrive, err, t0, n, num_kv_heads);
   if (cudaGetLastError() != cudaSuccess) return DLLM_ECUDA;
-  AttnScratch sc{reinterpret_cast<float*>(D.scratch + L.part_o), reinterpret_cast<float*>(D.scratch + L.part_ml), arrive,
+  AttnScratch sc{reinterpret_cast<float*>(scratch + L.part_o), reinterpret_cast<float*>(scratch + L.part_ml), arrive,
                  splits};
   const float scale = (float)(1.0 / std::sqrt((double)head_dim));
-  if (op_attention(q, kcache, vcache, out, rows, n, num_q_heads, num_kv_heads, head_dim, max_pos, scale, sc, err,
-                   D.sms, st) != cudaSuccess)
+  if (op_attention(q, kcache, vcache, out, rows, n, num_q_heads, num_kv_heads, head_dim, max_pos, scale, sc, err, sms,
+                   st) != cudaSuccess)
     return DLLM_ECUDA;
   return DLLM_OK;
+}
+
+extern "C" int dllm_attention_noalloc_status(void* cuda_stream, int timeout_ms, int* device_error) {
+  using namespace dllm;
+  if (device_error) *device_error = 0;
+  cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+  // bounded wait for the stream (the same polling the ctx calls use)
+  const auto t_end = std::chrono::steady_clock::now() + std::chrono::milliseconds(timeout_ms > 0 ? timeout_ms : 15000);
+  for (;;) {
+    const cudaError_t q = cudaStreamQuery(st);
+    if (q == cudaSuccess) break;
+    if (q != cudaErrorNotReady) return DLLM_ECUDA;
+    if (std::chrono::steady_clock::now() > t_end) return DLLM_ETIMEOUT;
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+  int v = 0;
+  if (cudaMemcpyFromSymbolAsync(&v, g_noalloc_scratch, sizeof(int), 0, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return DLLM_ECUDA;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return DLLM_ECUDA;
+  if (device_error) *device_error = v;
+  if (v == 0) return DLLM_OK;
+  if (v == kErrBarrier) return DLLM_ETIMEOUT;
+  if (v == kErrKvRange) return DLLM_ERANGE;
+  return DLLM_EDEVICE;
 }

@@ -186,14 +186,9 @@ def bench_pipeline(args, bench):
     tick_s = ms / 1000.0 / (args.steps * B)
     peak, peak_kind = bench.measured_peaks()
     achieved = max(stage_bytes) / tick_s / 1e9
-    # DRAM traffic of the slowest stage's launch: the committed ncu traffic /
-    # algorithmic ratio of the whole-model token applied to the stage's bytes
-    full_traffic = bench.traffic_from_profile()
-    traffic = None
-    if full_traffic is not None and args.model == "qwen2.5-7b":
-        full_alg = bench.token_bytes(cfg.with_(kv_dtype="bf16"), cfg.num_layers, head=True, embed=True,
-                                     kv_positions=args.kv_len + args.warmup + args.steps / 2)
-        traffic = max(stage_bytes) * full_traffic / full_alg
+    # DRAM traffic of the slowest stage's launch: the ncu traffic / algorithmic
+    # ratio of the profiled whole-model token applied to the stage's bytes
+    traffic = bench.traffic_bytes(max(stage_bytes), args.model)
     # e2e: the same loop with every tick's tokens copied to the host and checked
     e2e = None
     res = None

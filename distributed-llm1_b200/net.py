@@ -57,8 +57,8 @@ class FrameServer:
             while not self._stop.is_set():
                 try:
                     data = recv_frame(conn)
-                except (ConnectionError, OSError):
-                    return
+                except (ConnectionError, OSError, ValueError):
+                    return  # closed, or an oversized / malformed frame: drop the connection
                 try:
                     with self._lock:
                         reply = self.handler(data)

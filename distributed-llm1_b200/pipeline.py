@@ -196,6 +196,16 @@ class Stage:
                       "read_trace")
         return out
 
+    def read_workspace(self, which: str, rows: int = 1) -> np.ndarray:
+        """Latest pass's q (after bias + RoPE), attention output or SiLU(gate)*up
+        of the stage's last layer, [rows, width] fp32 (test hook)."""
+        idx = {"q": 0, "att": 1, "mid": 2}[which]
+        width = self.k.cfg.intermediate_size if which == "mid" else self.k.NQ * self.k.HD
+        out = np.empty((rows, width), np.float32)
+        self.k._check(self.lib.dllm_stage_read_workspace(self.handle, idx, rows, _lib.ptr(out, C.c_float)),
+                      "read_workspace")
+        return out
+
     def pages_per_seq(self) -> int:
         return int(self.lib.dllm_stage_pages_per_seq(self.handle))
 

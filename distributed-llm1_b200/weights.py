@@ -139,8 +139,29 @@ def load_checkpoint(kctx, path: str, start: int, end: int, stage=None, leader=No
     weights.js:167-182), one tensor at a time from the memory-mapped file to the
     device, so the host holds one tensor at most. `stage` receives the layer
     tensors (`stage.W[name]`); `leader` (a LeaderPipeline) the embedding, final
-    norm and, for untied models, `lm_head.weight`. Returns the names uploaded;
-    names the checkpoint lacks (e.g. biases of a bias-free model) are skipped."""
+    norm and, for untied models, `lm_head.weight`. Returns the names uploaded.
+    Only the q/k/v projection biases (absent in bias-free models) and
+    `lm_head.weight` (absent when the embeddings are tied) may be missing; any
+    other missing tensor raises KeyError, and every tensor's element count is
+    checked against the context's model config before it is uploaded (a
+    truncated or mis-sharded checkpoint fails here, not in a later kernel)."""
+    cfg = kctx.cfg
+    D, QD, KD, I, V = (cfg.hidden_size, cfg.num_q_heads * cfg.head_dim, cfg.num_kv_heads * cfg.head_dim,
+                       cfg.intermediate_size, cfg.vocab_size)
+    sizes = {"input_layernorm.weight": D, "post_attention_layernorm.weight": D,
+             "self_attn.q_proj.weight": QD * D, "self_attn.k_proj.weight": KD * D,
+             "self_attn.v_proj.weight": KD * D, "self_attn.o_proj.weight": D * QD,
+             "self_attn.q_proj.bias": QD, "self_attn.k_proj.bias": KD, "self_attn.v_proj.bias": KD,
+             "mlp.gate_proj.weight": I * D, "mlp.up_proj.weight": I * D, "mlp.down_proj.weight": D * I,
+             "model.embed_tokens.weight": V * D, "model.norm.weight": D, "lm_head.weight": V * D}
+
+    def expected(name: str) -> int:
+        key = name.split(".", 3)[3] if name.startswith("model.layers.") else name
+        return sizes[key]
+
+    def optional(name: str) -> bool:
+        return name.endswith("_proj.bias") or name == "lm_head.weight"
+
     where = {}
     maps = {}
     for f in checkpoint_files(path):
@@ -152,8 +173,13 @@ def load_checkpoint(kctx, path: str, start: int, end: int, stage=None, leader=No
     def one(name):
         f = where.get(name)
         if f is None:
-            return None
+            if optional(name):
+                return None
+            raise KeyError(f"checkpoint {path} has no tensor {name}")
         bits = read_tensors(f, [name], maps[f])[name]
+        if bits.size != expected(name):
+            raise ValueError(f"{name}: {bits.size} elements in the checkpoint, the model config needs "
+                             f"{expected(name)}")
         buf = kctx.loadWeightBf16(bits, name)
         done.append(name)
         return buf

@@ -173,6 +173,12 @@ int dllm_stage_fill_kv_random(dllm_stage* st, int seq, int n_slots, uint64_t see
  * distinct and < max_seqs * pages_per_seq). Test hook for the paged layout. */
 int dllm_stage_set_page_table(dllm_stage* st, int seq, const int32_t* pages, int n_pages);
 int dllm_stage_pages_per_seq(const dllm_stage* st);
+/* Reads the latest pass's per-row workspace of the stage's last layer: which 0 =
+ * q after bias and RoPE [rows, NQ*HD] (the input of ctx.attention,
+ * pipeline.js:62-65), 1 = attention output [rows, NQ*HD] (pipeline.js:65),
+ * 2 = SiLU(gate)*up [rows, I] (pipeline.js:72). Test hook for op-level checks of
+ * the fused phases (the reference creates one buffer per op, kernels.js:222-301). */
+int dllm_stage_read_workspace(dllm_stage* st, int which, int rows, float* dst);
 /* Tracing (the reference logs performance.now() deltas, pipeline.js:144,158,172):
  * with cap > 0 every stage-kernel launch stamps the GPU global timer (ns) at
  * its start and after each grid barrier into a device buffer of `cap` entries
@@ -226,18 +232,30 @@ int dllm_leader_read_logits(dllm_leader* ld, int index, float* out);
  * cudaMalloc/cudaFree (which may synchronise the device). Same math as
  * dllm_attention (kernels.js:86-132 semantics; caches [max_pos, KVH*HD] fp32,
  * row t attends slots [0, t0+t]), but the caller passes every buffer as a device
- * pointer and the split partials, ticket counters and row descriptors live in a
- * 4 MiB static device array that every GPU loading this library holds until the
- * process exits. No ctx is needed; work is enqueued on `cuda_stream` (NULL: the
- * legacy default stream) and the call does not wait for it.
- * The first call on a device, with that device current, resolves the array's
- * device address and sets the kernel's shared-memory limit; make that first call
- * before any latency-sensitive work. Calls share the array: calls that overlap
- * on the GPU (other streams, other threads) race. Limits: 1 <= n <= 64 rows
+ * pointer and the split partials, ticket counters, row descriptors and error word
+ * live in a 4 MiB static device array that every GPU loading this library holds
+ * until the process exits. No ctx is needed; work is enqueued on `cuda_stream`
+ * (NULL: the legacy default stream) and the call does not wait for it.
+ * Each call, with the caller's device current, resolves the array's device address
+ * and sets the kernel's shared-memory limit (cheap, allocation-free, nothing cached,
+ * so a device reset between calls is harmless). Calls share the array: calls that
+ * overlap on the GPU (other streams, other threads) race. Limits: 1 <= n <= 64 rows
  * (DLLM_ERANGE beyond), head_dim 64 or 128, at most 8 query heads per KV head
- * (DLLM_EINVAL otherwise). */
+ * (DLLM_EINVAL otherwise).
+ * The return value covers the arguments and the launch only. Errors the kernels
+ * find on the device (a split-merge wait that ran out, a row outside the cache)
+ * are read with dllm_attention_noalloc_status after the call and before the next
+ * one (the next call clears them). */
 int dllm_attention_noalloc(const float* q, const float* kcache, const float* vcache, float* out, int t0, int n,
                            int num_q_heads, int num_kv_heads, int head_dim, int max_pos, void* cuda_stream);
+/* Waits (bounded by timeout_ms, <= 0: 15000) for `cuda_stream`, then reads the
+ * device error word of the latest dllm_attention_noalloc on the current device.
+ * Returns DLLM_OK when the kernels reported nothing, DLLM_ETIMEOUT when a split
+ * merge gave up waiting (or the stream wait itself timed out), DLLM_ERANGE when a
+ * row fell outside the cache, DLLM_EDEVICE for other device codes; the raw device
+ * code goes to *device_error (may be NULL). Allocates nothing. No counterpart in
+ * the reference (readF32's bounded wait, kernels.js:201-207, is the model). */
+int dllm_attention_noalloc_status(void* cuda_stream, int timeout_ms, int* device_error);
 
 #ifdef __cplusplus
 }

@@ -266,6 +266,22 @@ void ref_model_fill_kv(void* h, int n, uint64_t seed) {
   m->T0 = n;
 }
 
+// Load KV rows into slots [slot0, slot0 + n) of local layer `layer` (which: 0 = K,
+// 1 = V) from src [n][KVH*HD] fp32, bf16-rounded when the cache is bf16. Lets a
+// check start from the exact cache contents another implementation holds.
+int ref_model_set_kv(void* h, int layer, int which, int slot0, int n, const float* src) {
+  auto* m = (RefModel*)h;
+  if (layer < 0 || layer >= (int)m->kk.size() || slot0 < 0 || n < 0 || slot0 + n > m->max_pos) return -1;
+  const size_t row = (size_t)m->KVH * m->HD;
+  std::vector<float>& dst = which ? m->vv[layer] : m->kk[layer];
+  for (size_t i = 0; i < (size_t)n * row; ++i) {
+    float a = src[i];
+    if (m->kv_bf16) a = bf(to_bf16(a));
+    dst[(size_t)slot0 * row + i] = a;
+  }
+  return 0;
+}
+
 // Stage.forward (pipeline.js:48-78): h [n][D] in place. Returns 0, or -1 on KV overflow.
 int ref_stage_forward(void* hm, float* h, int n, int pos_start) {
   auto* m = (RefModel*)hm;

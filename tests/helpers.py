@@ -118,6 +118,10 @@ def ref_lib():
     lib.ref_sample_last.argtypes = [C.c_void_p, F, F]
     lib.ref_generate.argtypes = [C.c_void_p, I, C.c_int, C.c_int, C.c_int, I, F]
     lib.ref_model_fill_kv.argtypes = [C.c_void_p, C.c_int, C.c_uint64]
+    lib.ref_model_set_kv.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, F]
+    lib.ref_model_set_t0.argtypes = [C.c_void_p, C.c_int]
+    lib.ref_model_t0.argtypes = [C.c_void_p]
+    lib.ref_embed.argtypes = [C.c_void_p, I, C.c_int, F]
     lib.ref_fill_normal_bf16.argtypes = [U16, C.c_size_t, C.c_uint64, C.c_float]
     return lib
 
@@ -157,6 +161,32 @@ class RefModel:
         h = np.ascontiguousarray(hidden, np.float32).reshape(-1).copy()
         assert self.lib.ref_stage_forward(self.h, h.ctypes.data_as(C.POINTER(C.c_float)), n, pos_start) == 0
         return h
+
+    def set_kv(self, layer: int, which: int, slot0: int, rows):
+        a = np.ascontiguousarray(rows, np.float32)
+        assert self.lib.ref_model_set_kv(self.h, layer, which, slot0, a.shape[0],
+                                         a.ctypes.data_as(C.POINTER(C.c_float))) == 0
+
+    @property
+    def T0(self) -> int:
+        return int(self.lib.ref_model_t0(self.h))
+
+    @T0.setter
+    def T0(self, v: int):
+        self.lib.ref_model_set_t0(self.h, int(v))
+
+    def decode_step(self, token: int):
+        """One greedy step at position == slot == T0 (the decode branch of
+        pipeline.js:262-267): embed, layers, final norm + LM head; returns
+        (next token, logits)."""
+        t = np.array([token], np.int32)
+        h = np.zeros(self.cfg.hidden_size, np.float32)
+        self.lib.ref_embed(self.h, t.ctypes.data_as(C.POINTER(C.c_int)), 1, h.ctypes.data_as(C.POINTER(C.c_float)))
+        h = self.forward(h, 1, self.T0)
+        lg = np.zeros(self.cfg.vocab_size, np.float32)
+        tok = self.lib.ref_sample_last(self.h, h.ctypes.data_as(C.POINTER(C.c_float)),
+                                       lg.ctypes.data_as(C.POINTER(C.c_float)))
+        return int(tok), lg
 
     def generate(self, tokens, max_new, keep_logits=False):
         t = np.ascontiguousarray(tokens, np.int32)

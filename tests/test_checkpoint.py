@@ -27,7 +27,8 @@ def write_sharded(dirpath, W):
 
 class FakeCtx:
     """Records uploads instead of calling the library (CPU test)."""
-    def __init__(self):
+    def __init__(self, cfg):
+        self.cfg = cfg
         self.up = {}
 
     def loadWeightBf16(self, bits, name):
@@ -52,7 +53,7 @@ def test_checkpoint_slice_roundtrip(tmp_path, dllm, weights_cache):
     files = dllm.weights.checkpoint_files(str(tmp_path))
     assert [os.path.basename(f) for f in files] == ["model-00001-of-00002.safetensors",
                                                     "model-00002-of-00002.safetensors"]
-    ctx, st, ld = FakeCtx(), FakeStage(), FakeLeader()
+    ctx, st, ld = FakeCtx(cfg), FakeStage(), FakeLeader()
     done = dllm.load_checkpoint(ctx, str(tmp_path), 1, 2, stage=st, leader=ld)
     want = dllm.tensorsForLayers(1, 2, False)
     assert sorted(st.W) == sorted(want)
@@ -69,10 +70,41 @@ def test_checkpoint_single_file_and_missing_biases(tmp_path, dllm):
     path = str(tmp_path / "model.safetensors")
     dllm.weights.write_safetensors(path, W)
     assert dllm.weights.checkpoint_files(path) == [path]
-    ctx, st = FakeCtx(), FakeStage()
+    ctx, st = FakeCtx(cfg), FakeStage()
     dllm.load_checkpoint(ctx, path, 0, cfg.num_layers, stage=st)
     assert not any(n.endswith("_proj.bias") for n in st.W)  # bias-free checkpoints load without them
     assert len(st.W) == 9 * cfg.num_layers
+
+
+def test_checkpoint_missing_required_tensor_raises(tmp_path, dllm):
+    """Only the projection biases and an untied LM head may be absent: a checkpoint
+    without a required weight fails at load time with the tensor's name."""
+    cfg = oracle_cfg("tiny")
+    W = synth.synthetic_weights(cfg, seed=5)
+    del W["model.layers.1.mlp.down_proj.weight"]
+    path = str(tmp_path / "model.safetensors")
+    dllm.weights.write_safetensors(path, W)
+    with pytest.raises(KeyError, match="model.layers.1.mlp.down_proj.weight"):
+        dllm.load_checkpoint(FakeCtx(cfg), path, 0, cfg.num_layers, stage=FakeStage())
+    W2 = synth.synthetic_weights(cfg, seed=5)
+    del W2["model.norm.weight"]
+    dllm.weights.write_safetensors(path, W2)
+    with pytest.raises(KeyError, match="model.norm.weight"):
+        dllm.load_checkpoint(FakeCtx(cfg), path, 0, 1, stage=FakeStage(), leader=FakeLeader())
+
+
+def test_checkpoint_wrong_size_raises(tmp_path, dllm):
+    """A tensor whose element count disagrees with the model config (a truncated
+    or mis-sharded file) is rejected before upload."""
+    cfg = oracle_cfg("tiny")
+    W = synth.synthetic_weights(cfg, seed=6)
+    W["model.layers.0.self_attn.k_proj.weight"] = W["model.layers.0.self_attn.k_proj.weight"][:-8]
+    path = str(tmp_path / "model.safetensors")
+    dllm.weights.write_safetensors(path, W)
+    ctx = FakeCtx(cfg)
+    with pytest.raises(ValueError, match="k_proj.weight"):
+        dllm.load_checkpoint(ctx, path, 0, cfg.num_layers, stage=FakeStage())
+    assert "model.layers.0.self_attn.k_proj.weight" not in ctx.up
 
 
 @pytest.mark.gpu

@@ -67,14 +67,36 @@ def test_bad_frame_size_rejected(dllm):
         dllm.frames.unpack(b"\x00" * 18)  # rtc.js:17
 
 
+def test_oversized_frame_closes_connection(dllm):
+    """A length prefix beyond MAX_FRAME_BYTES makes the server drop the connection
+    (no exception escapes its thread); the server keeps serving new connections."""
+    import struct
+    srv = dllm.FrameServer(echo_stage(dllm)).start()
+    try:
+        s = socket.create_connection(("127.0.0.1", srv.port), timeout=5.0)
+        s.sendall(struct.pack("<Q", dllm.net.MAX_FRAME_BYTES + 1))
+        assert s.recv(16) == b""  # closed by the server
+        s.close()
+        tr = dllm.TcpTransport({0: ("127.0.0.1", srv.port)}, timeout=5.0)
+        x = np.arange(8, dtype=np.float32)
+        resp = dllm.frames.unpack(tr(0, dllm.frames.pack(dllm.FRAME["HIDDEN_REQ"], 2, 0, x)))
+        np.testing.assert_array_equal(resp["f32"], x + 1.0)
+        tr.close()
+    finally:
+        srv.stop()
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("via", ["local", "tcp"])
 def test_two_stage_leader_matches_single_node(dllm, weights_cache, via):
     """Leader owns layers [0, 1) + head; a second Stage owns [1, 2) behind the
-    transport. Greedy tokens equal the single-node generate."""
+    transport. Greedy tokens equal the oracle's generate (pipeline.js:255-281 on
+    the CPU restatement) and the single-node generate."""
+    import ref_forward as ref
     cfg = oracle_cfg("tiny")
     W = get_weights(weights_cache, "tiny", cfg)
     prompt, steps = [11, 200, 37, 5], 6
+    oracle_tokens, _ = ref.OracleLeader(cfg, ref.Weights(W), "f32").generate(prompt, steps)
     ctx1, single = build_leader(dllm, cfg, W, "f32")
     want = []
     single.onToken = want.append
@@ -97,6 +119,7 @@ def test_two_stage_leader_matches_single_node(dllm, weights_cache, via):
     ld.onToken = got.append
     ld.generate(prompt, steps)
     try:
+        assert got == list(oracle_tokens)
         assert got == want
         assert remote.T0 == len(prompt) + steps - 1
     finally:

@@ -4,24 +4,45 @@ or a latency-critical loop that cannot afford cudaMalloc/cudaFree). The caller
 passes device pointers; the entry point's scratch is a static device array.
 
 Checked through the C ABI against the allocating entry point (dllm_attention)
-on two calls in a row, the second with a different shape so that stale scratch
-contents (ticket counters, partials) would show. This file is collected last."""
+and against the oracle's attention (kernels.js:86-132 restated in C++), on
+calls in a row whose shapes differ so that stale scratch contents (ticket
+counters, partials) would show, and with the device error word read back after
+every call. The shapes reach every path of the entry point: one row, a few rows,
+64 rows (the row limit, several work items per CTA and their split waits), head
+dims 128 and 64. This file is collected last."""
 import ctypes as C
 
 import numpy as np
 import pytest
 
-from helpers import assert_close, model_config, oracle_cfg
+from helpers import assert_close, model_config, oracle_cfg, ref_lib
 
 pytestmark = pytest.mark.gpu
 
-NQ, KVH, HD, MAX_POS = 12, 2, 128, 4096
+MAX_POS = 4096
 
 
-def test_no_alloc_attention_matches_allocating_entry_point(dllm):
+def _noalloc(lib, q, kt, vt, t0, n, nq, kvh, hd):
+    import torch
+    out = torch.full((n * nq * hd,), float("nan"), dtype=torch.float32, device="cuda")
+    st = torch.cuda.current_stream()
+    rc = lib.dllm_attention_noalloc(q.data_ptr(), kt.data_ptr(), vt.data_ptr(), out.data_ptr(), t0, n, nq, kvh, hd,
+                                    MAX_POS, C.c_void_p(st.cuda_stream))
+    assert rc == 0
+    code = C.c_int32(-1)
+    assert lib.dllm_attention_noalloc_status(C.c_void_p(st.cuda_stream), 15000, C.byref(code)) == 0
+    assert code.value == 0  # no device-side error reported
+    return out.cpu().numpy()
+
+
+@pytest.mark.parametrize("model", ["1.5b", "0.5b"])  # head_dim 128 (12/2 heads), 64 (14/2 heads)
+def test_no_alloc_attention_matches_allocating_entry_point(dllm, model):
     import torch
     lib = dllm.load_library()
-    ctx = dllm.initKernels(0, model_config(dllm, oracle_cfg("1.5b")))
+    oc = oracle_cfg(model)
+    NQ, KVH, HD = oc.num_q_heads, oc.num_kv_heads, oc.head_dim
+    ctx = dllm.initKernels(0, model_config(dllm, oc))
+    rlib = ref_lib()
     rng = np.random.default_rng(11)
     kc = rng.standard_normal((MAX_POS, KVH * HD), dtype=np.float32)
     vc = rng.standard_normal((MAX_POS, KVH * HD), dtype=np.float32)
@@ -30,25 +51,26 @@ def test_no_alloc_attention_matches_allocating_entry_point(dllm):
     ctx.writeF32(vb, vc)
     kt = torch.from_numpy(kc).cuda()
     vt = torch.from_numpy(vc).cuda()
-    for t0, n in ((1500, 5), (37, 1)):
+    F = C.POINTER(C.c_float)
+    # two calls in a row of each shape: the second sees the first's scratch contents
+    for t0, n in ((1500, 5), (1500, 5), (37, 1), (3000, 64), (3000, 64), (0, 1)):
         q = rng.standard_normal(n * NQ * HD, dtype=np.float32)
         qb = ctx.createF32(q.size)
         ctx.writeF32(qb, q)
         want = ctx.readF32(ctx.attention(qb, kb, vb, t0, n), n * NQ * HD)
-        qt = torch.from_numpy(q).cuda()
-        out = torch.full((n * NQ * HD,), float("nan"), dtype=torch.float32, device="cuda")
-        st = torch.cuda.current_stream()
-        rc = lib.dllm_attention_noalloc(qt.data_ptr(), kt.data_ptr(), vt.data_ptr(), out.data_ptr(), t0, n, NQ, KVH,
-                                        HD, MAX_POS, C.c_void_p(st.cuda_stream))
-        assert rc == 0
-        torch.cuda.synchronize()
-        assert_close(out.cpu().numpy(), want, rtol=1e-5, atol=1e-6, what=f"noalloc attention t0={t0} n={n}")
+        got = _noalloc(lib, torch.from_numpy(q).cuda(), kt, vt, t0, n, NQ, KVH, HD)
+        assert_close(got, want, rtol=1e-5, atol=1e-6, what=f"noalloc vs dllm_attention t0={t0} n={n}")
+        ref = np.zeros(n * NQ * HD, np.float32)
+        rlib.ref_attention(q.ctypes.data_as(F), kc.ctypes.data_as(F), vc.ctypes.data_as(F), ref.ctypes.data_as(F),
+                           t0, n, NQ, KVH, HD)
+        assert_close(got, ref, rtol=1e-4, atol=1e-5, what=f"noalloc vs oracle t0={t0} n={n}")
     ctx.close()
 
 
 def test_no_alloc_attention_rejects_out_of_limit(dllm):
     import torch
     lib = dllm.load_library()
+    NQ, KVH, HD = 12, 2, 128
     buf = torch.zeros(128 * NQ * HD, dtype=torch.float32, device="cuda")
     p = buf.data_ptr()
     # 65 rows exceed the static scratch's row limit
