@@ -62,6 +62,7 @@ SIGNATURES = {
     "dllm_ctx_set_stream": (C.c_int, [P, P]),
     "dllm_ctx_synchronize": (C.c_int, [P, C.c_int]),
     "dllm_ctx_launch_count": (C.c_uint64, [P]),
+    "dllm_ctx_set_tensor_core_rows": (C.c_int, [P, C.c_int]),
     "dllm_load_weight_bits": (C.c_int, [P, U32P, C.c_size_t, C.c_char_p, PP]),
     "dllm_load_weight_bf16": (C.c_int, [P, U16P, C.c_size_t, C.c_char_p, PP]),
     "dllm_create_f32": (C.c_int, [P, C.c_size_t, C.c_char_p, PP]),
@@ -113,6 +114,14 @@ SIGNATURES = {
     "dllm_leader_set_keep_logits": (C.c_int, [P, C.c_int]),
     "dllm_leader_last_logits": (C.c_int, [P, F32P]),
     "dllm_leader_read_logits": (C.c_int, [P, C.c_int, F32P]),
+    "dllm_pipeline_create": (C.c_int, [P, C.c_int, C.c_int, C.c_int, C.c_int, PP]),
+    "dllm_pipeline_destroy": (None, [P]),
+    "dllm_pipeline_handle": (C.c_int, [P, C.POINTER(C.c_uint8)]),
+    "dllm_pipeline_connect": (C.c_int, [P, C.POINTER(C.c_uint8)]),
+    "dllm_pipeline_set_tokens": (C.c_int, [P, I32P, C.c_int]),
+    "dllm_pipeline_run": (C.c_int, [P, C.c_int]),
+    "dllm_pipeline_read_tokens": (C.c_int, [P, I32P, C.c_int]),
+    "dllm_pipeline_synchronize": (C.c_int, [P, C.c_int]),
     "dllm_attention_noalloc": (C.c_int, [P, P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, P]),
     "dllm_attention_noalloc_status": (C.c_int, [P, C.c_int, I32P]),
 }

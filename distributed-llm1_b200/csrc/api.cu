@@ -19,6 +19,7 @@
 #include <vector>
 
 #include "dllm.h"
+#include "gemm_tc.cuh"
 #include "kernels.cuh"
 #include "ops.cuh"
 #include "stage.cuh"
@@ -70,6 +71,10 @@ struct dllm_ctx {
   RowDesc* attn_rows = nullptr;
   unsigned long long* best = nullptr;  // argmax op
   unsigned long long* best_host = nullptr;
+  // tensor-core matmul: passes of >= tc_min_rows rows (0: never) and its scratch
+  int tc_min_rows = dllm::kTcMinRows;
+  void* tc_scratch = nullptr;
+  size_t tc_scratch_bytes = 0;
 };
 
 struct dllm_stage {
@@ -103,6 +108,15 @@ struct dllm_stage {
   float* hbuf = nullptr;
   size_t tokbuf_cap = 0;
   int32_t* tokbuf = nullptr;
+  // wide passes (> 8 rows, or >= the ctx's tensor-core rows): per-row workspaces
+  // for up to wide_cap rows; projections on the tensor cores, one launch per op
+  int wide_cap = 0, wide_splits = 1;
+  float *wq = nullptr, *wk = nullptr, *wv = nullptr, *watt = nullptr, *wg = nullptr, *wu = nullptr;
+  float *wpart_o = nullptr, *wpart_ml = nullptr;
+  unsigned int* warrive = nullptr;
+  RowDesc* wrows = nullptr;
+  float* wlogits = nullptr;  // [wide_cap][V], allocated when a wide pass samples tokens
+  unsigned long long* wbest = nullptr;
   // tracing: %globaltimer at kernel start and after every grid barrier (last launch)
   unsigned long long* trace = nullptr;
   int trace_cap = 0;
@@ -205,6 +219,9 @@ int sync_check(dllm_ctx* c, int timeout_ms) {
     if (code == dllm::kErrKvRange) return set_err(c, DLLM_ERANGE, "KV slot out of range (T0 + n > max_pos)");
     if (code == dllm::kErrBarrier) return set_err(c, DLLM_ETIMEOUT, "device grid barrier timed out");
     if (code == dllm::kErrToken) return set_err(c, DLLM_EINVAL, "token id out of vocabulary range");
+    if (code == dllm::kErrPeerWait)
+      return set_err(c, DLLM_ETIMEOUT, "pipeline hop: the previous stage's rows did not arrive in time");
+    if (code == dllm::kErrTcWait) return set_err(c, DLLM_ETIMEOUT, "tensor-core matmul: a pipeline wait timed out");
     return set_err(c, DLLM_EDEVICE, "device error code %d", code);
   }
   return DLLM_OK;
@@ -455,6 +472,37 @@ StageParams base_params(dllm_stage* s) {
   return P;
 }
 
+// Grow the ctx's tensor-core scratch to `bytes` (synchronises the stream first).
+int ensure_tc_scratch(dllm_ctx* c, size_t bytes) {
+  if (bytes <= c->tc_scratch_bytes) return DLLM_OK;
+  CK(c, cudaStreamSynchronize(c->stream));
+  dev_free(c->tc_scratch);
+  c->tc_scratch = nullptr;
+  c->tc_scratch_bytes = 0;
+  char* p = nullptr;
+  if (int rc = dev_alloc(c, &p, bytes, "tensor-core scratch")) return rc;
+  c->tc_scratch = p;
+  c->tc_scratch_bytes = bytes;
+  return DLLM_OK;
+}
+
+// y[t] (=|+=) rmsnorm?(x[t]) . W^T for n rows on the tensor cores, in launches of
+// up to kTcMaxRows rows (MATMUL, kernels.js:26-44, for n > 1).
+int tc_rows(dllm_ctx* c, const float* x, int n, int K, const __nv_bfloat16* w, int N, float* y, int accumulate,
+            const __nv_bfloat16* norm_w) {
+  for (int r0 = 0; r0 < n; r0 += dllm::kTcMaxRows) {
+    const int m = std::min(dllm::kTcMaxRows, n - r0);
+    const size_t need = dllm::tc_matmul_scratch_bytes(m, K, N, c->sms);
+    if (int rc = ensure_tc_scratch(c, need)) return rc;
+    cudaError_t e = dllm::tc_matmul(x + (size_t)r0 * K, m, K, w, N, y + (size_t)r0 * N, accumulate, norm_w,
+                                    c->cfg.rms_norm_eps, c->tc_scratch, c->tc_scratch_bytes, c->err_dev, c->sms,
+                                    c->stream);
+    if (e != cudaSuccess) return set_err(c, DLLM_ECUDA, "tensor-core matmul: %s", cudaGetErrorString(e));
+    c->launches += 2;
+  }
+  return DLLM_OK;
+}
+
 int launch(dllm_stage* s, StageParams& P) {
   dllm_ctx* c = s->ctx;
   int ms = c->sms / (P.m_rows * P.KVH);
@@ -467,9 +515,111 @@ int launch(dllm_stage* s, StageParams& P) {
   return DLLM_OK;
 }
 
-// Run n rows through the stage in passes of <= 8 rows: rows t = {seq, pos0 + t, T0 + t}.
+// Whether a pass of n rows takes the wide path (tensor-core projections).
+bool use_wide(const dllm_stage* s, int n) {
+  const int t = s->ctx->tc_min_rows;
+  return t > 0 && n >= t;
+}
+
+// Per-row workspaces of wide passes for up to `rows` rows (chunks of kTcMaxRows).
+int ensure_wide(dllm_stage* s, int rows, bool logits) {
+  dllm_ctx* c = s->ctx;
+  const dllm_config& f = c->cfg;
+  const int cap = std::min(rows, dllm::kTcMaxRows);
+  if (cap > s->wide_cap) {
+    CK(c, cudaStreamSynchronize(c->stream));
+    for (float** p : {&s->wq, &s->wk, &s->wv, &s->watt, &s->wg, &s->wu, &s->wpart_o, &s->wpart_ml, &s->wlogits}) {
+      dev_free(*p);
+      *p = nullptr;
+    }
+    dev_free(s->warrive);
+    dev_free(s->wrows);
+    dev_free(s->wbest);
+    s->warrive = nullptr;
+    s->wrows = nullptr;
+    s->wbest = nullptr;
+    s->wide_cap = 0;
+    const size_t R = cap, QD = (size_t)f.num_q_heads * f.head_dim, KD = (size_t)f.num_kv_heads * f.head_dim;
+    s->wide_splits = std::max(1, std::min(kMaxSplitsAlloc, c->sms / (dllm::kMaxRows * f.num_kv_heads)));
+    const size_t ms = s->wide_splits;
+    int rc = dev_alloc(c, &s->wq, R * QD, "wide q");
+    if (!rc) rc = dev_alloc(c, &s->wk, R * KD, "wide k");
+    if (!rc) rc = dev_alloc(c, &s->wv, R * KD, "wide v");
+    if (!rc) rc = dev_alloc(c, &s->watt, R * QD, "wide attention");
+    if (!rc) rc = dev_alloc(c, &s->wg, R * f.intermediate_size, "wide gate");
+    if (!rc) rc = dev_alloc(c, &s->wu, R * f.intermediate_size, "wide up");
+    if (!rc) rc = dev_alloc(c, &s->wpart_o, R * f.num_q_heads * ms * f.head_dim, "wide attention partials");
+    if (!rc) rc = dev_alloc(c, &s->wpart_ml, R * f.num_q_heads * ms * 2, "wide attention partials");
+    if (!rc) rc = dev_alloc(c, &s->warrive, 2 * R * f.num_kv_heads, "wide attention tickets");
+    if (!rc) rc = dev_alloc(c, &s->wrows, R, "wide rows");
+    if (!rc) rc = dev_alloc(c, &s->wbest, R, "wide argmax keys");
+    if (rc) return rc;
+    s->wide_cap = cap;
+  }
+  if (logits && !s->wlogits) {
+    if (int rc = dev_alloc(c, &s->wlogits, (size_t)s->wide_cap * f.vocab_size, "wide logits")) return rc;
+  }
+  return DLLM_OK;
+}
+
+// A wide pass of n rows (rd[t] = {seq, pos, slot}) over the stage's layers, one
+// kernel per op: RMSNorm + q|k|v projections on the tensor cores, bias + RoPE +
+// appendKv, attention over the paged cache, o_proj + residual, RMSNorm + gate|up,
+// SiLU(gate)*up, down_proj + residual (the op order of pipeline.js:52-75). With
+// tokens_in the rows start as token embeddings (pipeline.js:121-128); with
+// tokens_out each row ends with final norm + LM head + greedy argmax
+// (pipeline.js:141-174).
+int run_wide(dllm_stage* s, float* h, int n, const RowDesc* rd, const int32_t* tokens_in, int32_t* tokens_out) {
+  dllm_ctx* c = s->ctx;
+  const dllm_config& f = c->cfg;
+  const int D = f.hidden_size, QD = f.num_q_heads * f.head_dim, KD = f.num_kv_heads * f.head_dim,
+            I = f.intermediate_size;
+  if (int rc = ensure_wide(s, n, tokens_out != nullptr)) return rc;
+  const KvLayout kv = stage_kv(s);
+  for (int r0 = 0; r0 < n; r0 += s->wide_cap) {
+    const int m = std::min(s->wide_cap, n - r0);
+    float* hh = h + (size_t)r0 * D;
+    CK(c, cudaMemcpyAsync(s->wrows, rd + r0, sizeof(RowDesc) * m, cudaMemcpyHostToDevice, c->stream));
+    if (tokens_in) {
+      CK(c, dllm::op_embed(s->embed, tokens_in + r0, hh, m, D, f.vocab_size, c->err_dev, c->stream));
+      c->launches += 1;
+    }
+    for (int l = 0; l < s->nl; ++l) {
+      const LayerW& L = s->lw[l];
+      if (int rc = tc_rows(c, hh, m, D, L.wq, QD, s->wq, 0, L.ln1)) return rc;
+      if (int rc = tc_rows(c, hh, m, D, L.wk, KD, s->wk, 0, L.ln1)) return rc;
+      if (int rc = tc_rows(c, hh, m, D, L.wv, KD, s->wv, 0, L.ln1)) return rc;
+      CK(c, dllm::op_qkv_post(s->wq, s->wk, s->wv, L.bq, L.bk, L.bv, m, f.num_q_heads, f.num_kv_heads, f.head_dim,
+                              c->freq, s->wrows, kv, L.kc, L.vc, f.kv_dtype, c->err_dev, c->stream));
+      const dllm::AttnArgs A{s->wq, s->watt, L.kc, L.vc, kv, s->wrows, m, f.num_q_heads, f.num_kv_heads, c->scale,
+                             s->wide_splits, s->wpart_o, s->wpart_ml, s->warrive, c->err_dev};
+      CK(c, dllm::op_attention_paged(A, f.kv_dtype, f.head_dim, c->sms, c->stream));
+      if (int rc = tc_rows(c, s->watt, m, QD, L.wo, D, hh, 1, nullptr)) return rc;
+      if (int rc = tc_rows(c, hh, m, D, L.wg, I, s->wg, 0, L.ln2)) return rc;
+      if (int rc = tc_rows(c, hh, m, D, L.wu, I, s->wu, 0, L.ln2)) return rc;
+      CK(c, dllm::op_silu_mul(s->wg, s->wu, s->wg, m * I, c->stream));
+      if (int rc = tc_rows(c, s->wg, m, I, L.wd, D, hh, 1, nullptr)) return rc;
+      c->launches += 3;
+    }
+    if (tokens_out) {
+      if (int rc = tc_rows(c, hh, m, D, s->lm_head, f.vocab_size, s->wlogits, 0, s->norm)) return rc;
+      CK(c, dllm::op_argmax_rows(s->wlogits, m, f.vocab_size, s->wbest, tokens_out + r0, c->stream));
+      c->launches += 2;
+    }
+  }
+  return DLLM_OK;
+}
+
+// Run n rows through the stage: rows t = {seq, pos0 + t, T0 + t}. A wide pass on
+// the tensor cores when n reaches the ctx's tensor-core rows, else passes of <= 8
+// rows of the persistent stage kernel.
 int run_rows(dllm_stage* s, float* hrows, int n, int seq, int pos0, const int32_t* tokens_dev) {
   dllm_ctx* c = s->ctx;
+  if (use_wide(s, n)) {
+    std::vector<RowDesc> rd(n);
+    for (int t = 0; t < n; ++t) rd[t] = RowDesc{seq, pos0 + t, s->T0[seq] + t, 0};
+    return run_wide(s, hrows, n, rd.data(), tokens_dev, nullptr);
+  }
   for (int r0 = 0; r0 < n; r0 += dllm::kMaxRows) {
     const int m = std::min(dllm::kMaxRows, n - r0);
     RowDesc rd[dllm::kMaxRows];
@@ -537,6 +687,7 @@ void ctx_free(dllm_ctx* c) {
   dev_free(c->attn.part_ml);
   dev_free(c->attn.arrive);
   dev_free(c->attn_rows);
+  dev_free(c->tc_scratch);
   if (c->err_host) cudaFreeHost(c->err_host);
   if (c->best_host) cudaFreeHost(c->best_host);
   if (c->sync_event) cudaEventDestroy(c->sync_event);
@@ -659,6 +810,16 @@ int dllm_ctx_synchronize(dllm_ctx* c, int timeout_ms) {
 
 uint64_t dllm_ctx_launch_count(const dllm_ctx* c) { return c ? c->launches : 0; }
 
+int dllm_ctx_set_tensor_core_rows(dllm_ctx* c, int min_rows) {
+  if (!c) return DLLM_EINVAL;
+  if (min_rows != 0 && (min_rows < 2 || min_rows > dllm::kTcMaxRows))
+    return set_err(c, DLLM_EINVAL, "tensor_core_rows: %d outside 0 or [2, %d]", min_rows, dllm::kTcMaxRows);
+  if (min_rows != 0 && !dllm::tc_available())
+    return set_err(c, DLLM_ECUDA, "tensor_core_rows: the driver has no tensor-map encoder");
+  c->tc_min_rows = min_rows;
+  return DLLM_OK;
+}
+
 // ---- buffers -----------------------------------------------------------------------------
 int dllm_load_weight_bits(dllm_ctx* c, const uint32_t* bits, size_t n, const char* label, dllm_buf** out) {
   if (!c || !out) return DLLM_EINVAL;
@@ -777,6 +938,16 @@ int dllm_matmul(dllm_ctx* c, const dllm_buf* x, const dllm_buf* w, int n, int di
   if (int rc = use_device(c)) return rc;
   dllm_buf* o = nullptr;
   if (int rc = new_buf(c, (size_t)n * dout, 0, "mm_out", &o)) return rc;
+  if (c->tc_min_rows > 0 && n >= c->tc_min_rows) {
+    // a real GEMM: the tcgen05 path
+    if (int rc = tc_rows(c, (const float*)x->ptr, n, din, (const __nv_bfloat16*)w->ptr, dout, (float*)o->ptr, 0,
+                         nullptr)) {
+      dllm_buf_free(o);
+      return rc;
+    }
+    *out = o;
+    return DLLM_OK;
+  }
   cudaError_t e = dllm::op_matmul((const float*)x->ptr, (const __nv_bfloat16*)w->ptr, (float*)o->ptr, n, din, dout,
                                   c->sms, c->stream);
   if (e != cudaSuccess) {
@@ -1038,6 +1209,10 @@ void dllm_stage_destroy(dllm_stage* s) {
   dev_free(s->hbuf);
   dev_free(s->tokbuf);
   dev_free(s->trace);
+  for (float* p : {s->wq, s->wk, s->wv, s->watt, s->wg, s->wu, s->wpart_o, s->wpart_ml, s->wlogits}) dev_free(p);
+  dev_free(s->warrive);
+  dev_free(s->wrows);
+  dev_free(s->wbest);
   delete s;
   ctx_release(c);
 }
@@ -1102,9 +1277,9 @@ int dllm_stage_forward_rows(dllm_stage* s, float* h_dev, int m, const int32_t* s
                             int32_t* tokens_out_dev) {
   if (!s) return DLLM_EINVAL;
   dllm_ctx* c = s->ctx;
-  if (!h_dev || !seq_ids || m <= 0 || m > dllm::kMaxRows)
-    return set_err(c, DLLM_EINVAL, "forward_rows: need 1..%d rows", dllm::kMaxRows);
-  RowDesc rd[dllm::kMaxRows];
+  if (!h_dev || !seq_ids || m <= 0 || m > dllm::kTcMaxRows)
+    return set_err(c, DLLM_EINVAL, "forward_rows: need 1..%d rows", dllm::kTcMaxRows);
+  std::vector<RowDesc> rd(m);
   for (int i = 0; i < m; ++i) {
     const int q = seq_ids[i];
     if (q < 0 || q >= s->max_seqs) return set_err(c, DLLM_EINVAL, "forward_rows: invalid seq %d", q);
@@ -1120,14 +1295,23 @@ int dllm_stage_forward_rows(dllm_stage* s, float* h_dev, int m, const int32_t* s
   if (tokens_out_dev)
     if (int rc = need_head(s)) return rc;
   if (s->nl > 0 || tokens_in_dev || tokens_out_dev) {
-    CK(c, cudaMemcpyAsync(s->rows, rd, sizeof(RowDesc) * m, cudaMemcpyHostToDevice, c->stream));
-    StageParams P = base_params(s);
-    P.m_rows = m;
-    P.h = h_dev;
-    P.tokens_in = tokens_in_dev;
-    P.lm_head = tokens_out_dev ? s->lm_head : nullptr;
-    P.tokens_out = tokens_out_dev;
-    if (int rc = launch(s, P)) return rc;
+    if (use_wide(s, m)) {
+      if (int rc = run_wide(s, h_dev, m, rd.data(), tokens_in_dev, tokens_out_dev)) return rc;
+    } else {
+      // passes of <= 8 rows of the stage kernel (rows of distinct sequences are independent)
+      const size_t D = c->cfg.hidden_size;
+      for (int r0 = 0; r0 < m; r0 += dllm::kMaxRows) {
+        const int mm = std::min(dllm::kMaxRows, m - r0);
+        CK(c, cudaMemcpyAsync(s->rows, rd.data() + r0, sizeof(RowDesc) * mm, cudaMemcpyHostToDevice, c->stream));
+        StageParams P = base_params(s);
+        P.m_rows = mm;
+        P.h = h_dev + (size_t)r0 * D;
+        P.tokens_in = tokens_in_dev ? tokens_in_dev + r0 : nullptr;
+        P.lm_head = tokens_out_dev ? s->lm_head : nullptr;
+        P.tokens_out = tokens_out_dev ? tokens_out_dev + r0 : nullptr;
+        if (int rc = launch(s, P)) return rc;
+      }
+    }
   }
   for (int i = 0; i < m; ++i) s->T0[seq_ids[i]] += 1;
   return DLLM_OK;
@@ -1574,6 +1758,246 @@ int dllm_leader_read_logits(dllm_leader* ld, int index, float* out) {
   CK(c, cudaMemcpyAsync(out, ld->logits_ring + (size_t)index * c->cfg.vocab_size, (size_t)c->cfg.vocab_size * 4,
                         cudaMemcpyDeviceToHost, c->stream));
   return sync_check(c, kDefaultTimeoutMs);
+}
+
+// ---- multi-GPU pipeline: the layer-range stages of pipeline.js on one node ----------------
+// One process (or thread) per GPU, each holding one Stage. Micro-batch b = the
+// sequences [b * micro, (b + 1) * micro) circulates the ring rank 0 -> 1 -> ... ->
+// W-1 -> 0: the first stage embeds its tokens, every stage runs its layers, the
+// last stage samples the next tokens, which go back to the first stage. The hop
+// (pipeline.js:226-253; WebRTC frames in the reference) is fused into the stage
+// kernel: the pass ends by storing its output rows (or tokens) into the next
+// GPU's receive buffer over NVLink and releasing a per-micro-batch flag there;
+// the next stage's pass starts by waiting (bounded) on that flag. Receive
+// buffers are shared once through CUDA IPC handles the host exchanges. Flow
+// control comes from the ring itself: a stage writes micro-batch b again only
+// after b has gone around the ring, i.e. after the next stage finished with it.
+struct dllm_pipeline {
+  dllm_stage* st = nullptr;
+  dllm_ctx* ctx = nullptr;
+  int rank = 0, world = 1, n_micro = 1, micro = 1;
+  // receive buffer of this rank (one allocation, exported): h [B][m][D] f32,
+  // tokens [B][m] i32, flags [B] u32
+  char* rx = nullptr;
+  size_t rx_bytes = 0, off_tok = 0, off_flag = 0;
+  char* peer_rx = nullptr;  // the next rank's receive buffer (IPC mapping), or rx itself for one rank
+  float* h0 = nullptr;      // first stage: [B][m][D] work rows
+  int32_t* tok_out = nullptr;  // last stage: [B][m] sampled tokens
+  RowDesc* rows = nullptr;  // [B][m] device row descriptors, advanced on the device
+  int32_t* hist = nullptr;  // last stage: [hist_cap][B * m] tokens of the latest run
+  int hist_cap = 0, hist_steps = 0;
+  std::vector<unsigned int> passes;  // passes run per micro-batch
+  bool connected = false;
+};
+
+namespace {
+float* rx_h(const dllm_pipeline* pl, char* base, int b) {
+  return reinterpret_cast<float*>(base) + (size_t)b * pl->micro * pl->ctx->cfg.hidden_size;
+}
+int32_t* rx_tok(const dllm_pipeline* pl, char* base, int b) {
+  return reinterpret_cast<int32_t*>(base + pl->off_tok) + (size_t)b * pl->micro;
+}
+unsigned int* rx_flag(const dllm_pipeline* pl, char* base, int b) {
+  return reinterpret_cast<unsigned int*>(base + pl->off_flag) + b;
+}
+}  // namespace
+
+void dllm_pipeline_destroy(dllm_pipeline* pl) {
+  if (!pl) return;
+  dllm_ctx* c = pl->ctx;
+  cudaSetDevice(c->device);
+  cudaStreamSynchronize(c->stream);
+  if (pl->peer_rx && pl->peer_rx != pl->rx) cudaIpcCloseMemHandle(pl->peer_rx);
+  dev_free(pl->rx);
+  dev_free(pl->h0);
+  dev_free(pl->tok_out);
+  dev_free(pl->rows);
+  dev_free(pl->hist);
+  delete pl;
+  ctx_release(c);
+}
+
+int dllm_pipeline_create(dllm_stage* s, int rank, int world, int n_micro, int micro, dllm_pipeline** out) {
+  if (!s || !out) return DLLM_EINVAL;
+  *out = nullptr;
+  dllm_ctx* c = s->ctx;
+  const dllm_config& f = c->cfg;
+  if (world < 1 || rank < 0 || rank >= world) return set_err(c, DLLM_EINVAL, "pipeline: rank %d of %d", rank, world);
+  if (n_micro < 1 || micro < 1 || micro > dllm::kMaxRows)
+    return set_err(c, DLLM_EINVAL, "pipeline: need n_micro >= 1 and 1..%d sequences per micro-batch", dllm::kMaxRows);
+  if ((long long)n_micro * micro > s->max_seqs)
+    return set_err(c, DLLM_EINVAL, "pipeline: %d x %d sequences > the stage's max_seqs %d", n_micro, micro,
+                   s->max_seqs);
+  if (int rc = use_device(c)) return rc;
+  if (int rc = resolve(s)) return rc;
+  if (rank == 0 && !s->embed) return set_err(c, DLLM_ENOTFOUND, "pipeline: the first stage needs model.embed_tokens.weight");
+  if (rank == world - 1)
+    if (int rc = need_head(s)) return rc;
+  auto* pl = new dllm_pipeline();
+  pl->st = s;
+  pl->ctx = c;
+  ctx_retain(c);
+  pl->rank = rank;
+  pl->world = world;
+  pl->n_micro = n_micro;
+  pl->micro = micro;
+  pl->passes.assign(n_micro, 0u);
+  const size_t D = f.hidden_size, B = n_micro, m = micro;
+  pl->off_tok = (B * m * D * 4 + 255) / 256 * 256;
+  pl->off_flag = pl->off_tok + (B * m * 4 + 255) / 256 * 256;
+  pl->rx_bytes = pl->off_flag + 256;
+  int rc = dev_alloc(c, &pl->rx, pl->rx_bytes, "pipeline receive buffer");
+  if (!rc && rank == 0) rc = dev_alloc(c, &pl->h0, B * m * D, "pipeline rows");
+  if (!rc && rank == world - 1) rc = dev_alloc(c, &pl->tok_out, B * m, "pipeline tokens");
+  if (!rc) rc = dev_alloc(c, &pl->rows, B * m, "pipeline rows");
+  if (!rc) {
+    std::vector<RowDesc> rd(B * m);
+    for (size_t i = 0; i < B * m; ++i) rd[i] = RowDesc{(int)i, s->T0[i], s->T0[i], 0};
+    cudaError_t e = cudaMemcpyAsync(pl->rows, rd.data(), rd.size() * sizeof(RowDesc), cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) rc = set_err(c, DLLM_ECUDA, "pipeline init: %s", cudaGetErrorString(e));
+  }
+  if (rc) {
+    dllm_pipeline_destroy(pl);
+    return rc;
+  }
+  if (world == 1) {
+    pl->peer_rx = pl->rx;
+    pl->connected = true;
+  }
+  *out = pl;
+  return DLLM_OK;
+}
+
+int dllm_pipeline_handle(const dllm_pipeline* pl, uint8_t* out) {
+  if (!pl || !out) return DLLM_EINVAL;
+  dllm_ctx* c = pl->ctx;
+  if (int rc = use_device(c)) return rc;
+  cudaIpcMemHandle_t h;
+  CK(c, cudaIpcGetMemHandle(&h, pl->rx));
+  static_assert(sizeof(cudaIpcMemHandle_t) == DLLM_PIPELINE_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(out, &h, sizeof(h));
+  return DLLM_OK;
+}
+
+int dllm_pipeline_connect(dllm_pipeline* pl, const uint8_t* next_handle) {
+  if (!pl) return DLLM_EINVAL;
+  dllm_ctx* c = pl->ctx;
+  if (pl->world == 1) return DLLM_OK;
+  if (!next_handle) return set_err(c, DLLM_EINVAL, "pipeline_connect: null handle");
+  if (pl->connected) return set_err(c, DLLM_EINVAL, "pipeline_connect: already connected");
+  if (int rc = use_device(c)) return rc;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, next_handle, sizeof(h));
+  void* p = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_err(c, DLLM_ECUDA, "pipeline_connect: %s", cudaGetErrorString(e));
+  }
+  pl->peer_rx = static_cast<char*>(p);
+  pl->connected = true;
+  return DLLM_OK;
+}
+
+int dllm_pipeline_set_tokens(dllm_pipeline* pl, const int32_t* tokens, int n) {
+  if (!pl) return DLLM_EINVAL;
+  dllm_ctx* c = pl->ctx;
+  if (pl->rank != 0) return set_err(c, DLLM_EINVAL, "pipeline_set_tokens: only the first stage takes tokens");
+  if (!tokens || n != pl->n_micro * pl->micro)
+    return set_err(c, DLLM_EINVAL, "pipeline_set_tokens: need %d tokens", pl->n_micro * pl->micro);
+  for (int i = 0; i < n; ++i)
+    if (tokens[i] < 0 || tokens[i] >= c->cfg.vocab_size)
+      return set_err(c, DLLM_EINVAL, "pipeline_set_tokens: token %d out of range", tokens[i]);
+  if (int rc = use_device(c)) return rc;
+  CK(c, cudaMemcpyAsync(rx_tok(pl, pl->rx, 0), tokens, (size_t)n * 4, cudaMemcpyHostToDevice, c->stream));
+  return sync_check(c, kDefaultTimeoutMs);
+}
+
+int dllm_pipeline_run(dllm_pipeline* pl, int steps) {
+  if (!pl) return DLLM_EINVAL;
+  dllm_ctx* c = pl->ctx;
+  dllm_stage* s = pl->st;
+  if (steps < 1) return set_err(c, DLLM_EINVAL, "pipeline_run: invalid steps=%d", steps);
+  if (!pl->connected) return set_err(c, DLLM_EINVAL, "pipeline_run: not connected to the next stage");
+  const int B = pl->n_micro, m = pl->micro, D = c->cfg.hidden_size;
+  for (int q = 0; q < B * m; ++q)
+    if (s->T0[q] + steps > s->max_slots)
+      return set_err(c, DLLM_ERANGE, "KV cache overflow: seq %d T0=%d + %d steps > maxPos=%d", q, s->T0[q], steps,
+                     s->max_slots);
+  if (int rc = use_device(c)) return rc;
+  if (int rc = resolve(s)) return rc;
+  const bool first = pl->rank == 0, last = pl->rank == pl->world - 1;
+  if (last) {
+    if (steps > pl->hist_cap) {
+      CK(c, cudaStreamSynchronize(c->stream));
+      dev_free(pl->hist);
+      pl->hist = nullptr;
+      pl->hist_cap = 0;
+      if (int rc = dev_alloc(c, &pl->hist, (size_t)steps * B * m, "pipeline token history")) return rc;
+      pl->hist_cap = steps;
+    }
+  }
+  for (int step = 0; step < steps; ++step) {
+    for (int b = 0; b < B; ++b) {
+      const unsigned int k = pl->passes[b];  // passes of b so far on this rank
+      StageParams P = base_params(s);
+      P.m_rows = m;
+      P.rows = pl->rows + (size_t)b * m;
+      P.advance_rows = 1;
+      if (first) {
+        P.h = pl->h0 + (size_t)b * m * D;
+        P.tokens_in = rx_tok(pl, pl->rx, b);
+        if (k > 0 && pl->world > 1) {  // tokens of the previous round, from the last stage
+          P.in_flag = rx_flag(pl, pl->rx, b);
+          P.in_expect = k;
+        }
+      } else {
+        P.h = rx_h(pl, pl->rx, b);
+        P.in_flag = rx_flag(pl, pl->rx, b);
+        P.in_expect = k + 1;
+      }
+      if (last) {
+        P.lm_head = s->lm_head;
+        P.tokens_out = pl->world == 1 ? rx_tok(pl, pl->rx, b) : pl->tok_out + (size_t)b * m;
+        if (pl->world > 1) {
+          P.out_tok = rx_tok(pl, pl->peer_rx, b);
+          P.out_flag = rx_flag(pl, pl->peer_rx, b);
+          P.out_value = k + 1;
+        }
+      } else {
+        P.lm_head = nullptr;
+        P.out_h = rx_h(pl, pl->peer_rx, b);
+        P.out_flag = rx_flag(pl, pl->peer_rx, b);
+        P.out_value = k + 1;
+      }
+      if (int rc = launch(s, P)) return rc;
+      if (last)
+        CK(c, cudaMemcpyAsync(pl->hist + ((size_t)step * B + b) * m, P.tokens_out, (size_t)m * 4,
+                              cudaMemcpyDeviceToDevice, c->stream));
+      pl->passes[b] = k + 1;
+      for (int i = 0; i < m; ++i) s->T0[b * m + i] += 1;
+    }
+  }
+  pl->hist_steps = last ? steps : 0;
+  return DLLM_OK;
+}
+
+int dllm_pipeline_read_tokens(dllm_pipeline* pl, int32_t* out, int steps) {
+  if (!pl) return DLLM_EINVAL;
+  dllm_ctx* c = pl->ctx;
+  if (pl->rank != pl->world - 1) return set_err(c, DLLM_EINVAL, "pipeline_read_tokens: only the last stage samples");
+  if (!out || steps < 1 || steps > pl->hist_steps)
+    return set_err(c, DLLM_EINVAL, "pipeline_read_tokens: %d steps requested, %d run", steps, pl->hist_steps);
+  if (int rc = use_device(c)) return rc;
+  CK(c, cudaMemcpyAsync(out, pl->hist, (size_t)steps * pl->n_micro * pl->micro * 4, cudaMemcpyDeviceToHost, c->stream));
+  return sync_check(c, std::max(kDefaultTimeoutMs, steps * 200));
+}
+
+int dllm_pipeline_synchronize(dllm_pipeline* pl, int timeout_ms) {
+  if (!pl) return DLLM_EINVAL;
+  if (int rc = use_device(pl->ctx)) return rc;
+  return sync_check(pl->ctx, timeout_ms);
 }
 
 }  // extern "C"

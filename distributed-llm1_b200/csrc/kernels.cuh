@@ -106,6 +106,36 @@ DLLM_DEV bool grid_barrier(unsigned int* count, int* err) {
   return s_ok != 0;
 }
 
+// System-scope (peer GPU) flag helpers for the pipeline hop over NVLink.
+DLLM_DEV unsigned int ld_acquire_sys_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+DLLM_DEV void st_release_sys_u32(unsigned int* p, unsigned int v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+constexpr int kErrPeerWait = 6;
+
+// Bounded wait of the whole CTA until *flag >= expect (written by another GPU).
+DLLM_DEV bool wait_peer_flag(const unsigned int* flag, unsigned int expect, int* err) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const long long t0 = clock64();
+    while ((int)(ld_acquire_sys_u32(flag) - expect) < 0) {
+      if (clock64() - t0 > kBarrierTimeoutCycles) {
+        atomicExch(err, kErrPeerWait);
+        ok = 0;
+        break;
+      }
+    }
+    s_ok = ok;
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+
 // ---- activation staging (RMSNorm prologue, kernels.js:46-63) -----------------------
 // Per row: ss = sum(x^2), scale = 1 / sqrt(ss / K + eps), x' = (x * scale) * g.
 struct GemvIn {
@@ -288,18 +318,23 @@ DLLM_DEV void gemv_phase(const Epi& epi, const GemvIn& in, int units, const Phas
   }
 }
 
-// Ask the TMA unit to pull up to `budget` bytes of this CTA's rows of a future
-// matvec phase into L2 (whole rows, in unit order). Issued by warp 0.
+// Ask the TMA unit to pull rows of this CTA's units of a future matvec phase
+// into L2: the units the phase will give CTA `cta` (the same unit_range split,
+// `align` included), in the order the phase reads them, starting `skip` bytes
+// into the CTA's share and covering up to `budget` bytes (whole units, at least
+// one when budget > 0). Issued by warp 0; the copies run in the background.
 template <class Epi>
-DLLM_DEV void prefetch_phase(const Epi& epi, int K, int units, int cta, int ncta, int budget) {
+DLLM_DEV void prefetch_phase(const Epi& epi, int K, int units, int cta, int ncta, int budget, int align = 1,
+                             int skip = 0) {
   if (budget <= 0 || (threadIdx.x >> 5) != 0) return;
   const int lane = threadIdx.x & 31;
-  const int u0 = (int)(((long long)cta * units) / ncta);
-  const int u1 = (int)(((long long)(cta + 1) * units) / ncta);
+  int u0, u1;
+  unit_range(units, cta, ncta, align, u0, u1);
   const int row_bytes = K * 2;
-  const int max_units = budget / (row_bytes * Epi::R);
-  const int uend = min(u1, u0 + max(1, max_units));
-  for (int u = u0 + lane; u < uend; u += 32) {
+  const int unit_bytes = row_bytes * Epi::R;
+  const int ubeg = u0 + skip / unit_bytes;
+  const int uend = min(u1, ubeg + max(1, budget / unit_bytes));
+  for (int u = ubeg + lane; u < uend; u += 32) {
     const uint4* p[Epi::R];
     epi.unit_rows(u, K, p);
 #pragma unroll

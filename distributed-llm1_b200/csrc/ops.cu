@@ -175,6 +175,148 @@ static cudaError_t launch_attention(const AttnArgs& A, int sms, cudaStream_t st)
   return cudaLaunchKernelEx(&cfg, attention_op_kernel<HD>, A);
 }
 
+// ---- ATTENTION over a stage's paged cache (wide passes) -----------------------------
+template <typename KT, int HD>
+__global__ void __launch_bounds__(kThreads, 1) attention_paged_kernel(const AttnArgs A) {
+  extern __shared__ __align__(16) float smem[];
+  attn_phase<KT, HD>(A, smem, blockIdx.x, gridDim.x);
+}
+
+template <typename KT, int HD>
+static cudaError_t launch_attention_paged(const AttnArgs& A, int sms, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(sms);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = sizeof(float) * (size_t)attn_smem_floats<KT, HD>();
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;  // split CTAs of a (row, kv head) wait for each other
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, attention_paged_kernel<KT, HD>, A);
+}
+
+cudaError_t op_attention_paged(const AttnArgs& A, int kv_dtype, int hd, int sms, cudaStream_t st) {
+  if (kv_dtype == 0) {
+    if (hd == 64) return launch_attention_paged<float, 64>(A, sms, st);
+    if (hd == 128) return launch_attention_paged<float, 128>(A, sms, st);
+  } else {
+    if (hd == 64) return launch_attention_paged<__nv_bfloat16, 64>(A, sms, st);
+    if (hd == 128) return launch_attention_paged<__nv_bfloat16, 128>(A, sms, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
+// ---- q|k|v epilogue of a wide pass: addBias, ropeQ/ropeK, appendKv -------------------
+// Thread per (row, head, half): the same arithmetic as the stage kernel's fused
+// epilogue (pipeline.js:59-64, kernels.js:66-83 and :148-159); k and v go to the
+// row's KV slot through the paged layout, q is rotated in place.
+template <typename KT>
+__global__ void qkv_post_kernel(float* q, const float* k, const float* v, const __nv_bfloat16* bq,
+                                const __nv_bfloat16* bk, const __nv_bfloat16* bv, int n, int NQ, int KVH, int HD,
+                                const float* freq, const RowDesc* rows, KvLayout kv, KT* kc, KT* vc, int* err) {
+  const int half_n = HD >> 1;
+  const int heads = NQ + 2 * KVH;
+  const long long total = (long long)n * heads * half_n;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int half = (int)(i % half_n);
+    const int hh = (int)((i / half_n) % heads);
+    const int t = (int)(i / ((long long)half_n * heads));
+    int kind, lh;
+    if (hh < NQ) {
+      kind = 0;
+      lh = hh;
+    } else if (hh < NQ + KVH) {
+      kind = 1;
+      lh = hh - NQ;
+    } else {
+      kind = 2;
+      lh = hh - NQ - KVH;
+    }
+    const int j0 = lh * HD + half, j1 = j0 + half_n;
+    const float* src = kind == 0 ? q + (size_t)t * NQ * HD : (kind == 1 ? k : v) + (size_t)t * KVH * HD;
+    float x1 = src[j0], x2 = src[j1];
+    const __nv_bfloat16* b = kind == 0 ? bq : (kind == 1 ? bk : bv);
+    if (b) {
+      x1 = __fadd_rn(x1, bf16_to_f32(b[j0]));
+      x2 = __fadd_rn(x2, bf16_to_f32(b[j1]));
+    }
+    const RowDesc rd = rows[t];
+    if (kind < 2) {
+      const float ang = __fmul_rn((float)rd.pos, freq[half]);
+      float sn, cs;
+      sincosf(ang, &sn, &cs);
+      const float o1 = __fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
+      const float o2 = __fadd_rn(__fmul_rn(x1, sn), __fmul_rn(x2, cs));
+      x1 = o1;
+      x2 = o2;
+    }
+    if (kind == 0) {
+      float* qr = q + (size_t)t * NQ * HD;
+      qr[j0] = x1;
+      qr[j1] = x2;
+      continue;
+    }
+    if (rd.slot < 0 || rd.slot >= kv.max_slots || rd.seq < 0 || rd.seq >= kv.num_seqs) {
+      atomicExch(err, kErrKvRange);
+      continue;
+    }
+    KT* base = (kind == 1 ? kc : vc) + kv.offset(rd.seq, rd.slot, lh);
+    base[half] = cvt_out<KT>(x1);
+    base[half + half_n] = cvt_out<KT>(x2);
+  }
+}
+
+cudaError_t op_qkv_post(float* q, const float* k, const float* v, const __nv_bfloat16* bq, const __nv_bfloat16* bk,
+                        const __nv_bfloat16* bv, int n, int NQ, int KVH, int HD, const float* freq,
+                        const RowDesc* rows, const KvLayout& kv, void* kc, void* vc, int kv_dtype, int* err,
+                        cudaStream_t st) {
+  const long long total = (long long)n * (NQ + 2 * KVH) * (HD / 2);
+  const unsigned int b = blocks_for(total, 256);
+  if (kv_dtype == 0)
+    qkv_post_kernel<float><<<b, 256, 0, st>>>(q, k, v, bq, bk, bv, n, NQ, KVH, HD, freq, rows, kv, (float*)kc,
+                                              (float*)vc, err);
+  else
+    qkv_post_kernel<__nv_bfloat16><<<b, 256, 0, st>>>(q, k, v, bq, bk, bv, n, NQ, KVH, HD, freq, rows, kv,
+                                                      (__nv_bfloat16*)kc, (__nv_bfloat16*)vc, err);
+  return cudaGetLastError();
+}
+
+// ---- greedy argmax of many rows (sampleLast per sequence, pipeline.js:159-162) --------
+__global__ void argmax_rows_kernel(const float* logits, int n, unsigned long long* best) {
+  __shared__ unsigned long long sb;
+  const int row = blockIdx.y;
+  if (threadIdx.x == 0) sb = 0ull;
+  __syncthreads();
+  unsigned long long k = 0ull;
+  const float* x = logits + (size_t)row * n;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const unsigned long long kk = argmax_key(x[i], i);
+    if (kk > k) k = kk;
+  }
+  if (k) atomicMax(&sb, k);
+  __syncthreads();
+  if (threadIdx.x == 0 && sb) atomicMax(best + row, sb);
+}
+__global__ void argmax_tokens_kernel(unsigned long long* best, int rows, int32_t* tokens) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r < rows) {
+    const unsigned long long k = best[r];
+    tokens[r] = k == 0ull ? 0 : argmax_key_index(k);  // all-NaN row: index 0 (the reference's initial best)
+    best[r] = 0ull;
+  }
+}
+
+cudaError_t op_argmax_rows(const float* logits, int rows, int n, unsigned long long* best, int32_t* tokens,
+                           cudaStream_t st) {
+  argmax_rows_kernel<<<dim3(64, rows), 256, 0, st>>>(logits, n, best);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  argmax_tokens_kernel<<<(rows + 127) / 128, 128, 0, st>>>(best, rows, tokens);
+  return cudaGetLastError();
+}
+
 cudaError_t configure_op_kernels() {
   const int mm = (int)kStageSmemBytes;
   cudaError_t e = cudaFuncSetAttribute(matmul_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, mm);
@@ -187,6 +329,18 @@ cudaError_t configure_op_kernels() {
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(attention_op_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)attn_smem_bytes<128>());
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attention_paged_kernel<float, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(sizeof(float) * attn_smem_floats<float, 64>()));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attention_paged_kernel<float, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(sizeof(float) * attn_smem_floats<float, 128>()));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attention_paged_kernel<__nv_bfloat16, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(sizeof(float) * attn_smem_floats<__nv_bfloat16, 64>()));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attention_paged_kernel<__nv_bfloat16, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(sizeof(float) * attn_smem_floats<__nv_bfloat16, 128>()));
   return e;
 }
 

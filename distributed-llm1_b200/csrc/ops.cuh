@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include "common.cuh"
+#include "kernels.cuh"
 
 namespace dllm {
 
@@ -34,6 +35,17 @@ struct AttnScratch {
 cudaError_t op_attention(const float* q, const float* kc, const float* vc, float* out, const RowDesc* rows, int n,
                          int nq, int kvh, int hd, int max_pos, float scale, const AttnScratch& sc, int* err, int sms,
                          cudaStream_t st);
+// ATTENTION over a stage's paged KV cache (the stage kernel's attention phase as
+// its own cooperative launch); A.kc/A.vc are the layer's pools, kv_dtype 0 fp32, 1 bf16
+cudaError_t op_attention_paged(const AttnArgs& A, int kv_dtype, int hd, int sms, cudaStream_t st);
+// addBias + ropeQ/ropeK + appendKv of n rows whose q|k|v projections are in q, k, v
+cudaError_t op_qkv_post(float* q, const float* k, const float* v, const __nv_bfloat16* bq, const __nv_bfloat16* bk,
+                        const __nv_bfloat16* bv, int n, int NQ, int KVH, int HD, const float* freq,
+                        const RowDesc* rows, const KvLayout& kv, void* kc, void* vc, int kv_dtype, int* err,
+                        cudaStream_t st);
+// greedy token of each of `rows` rows of n logits (best: [rows] keys, zero between uses)
+cudaError_t op_argmax_rows(const float* logits, int rows, int n, unsigned long long* best, int32_t* tokens,
+                           cudaStream_t st);
 // argmax over n logits into *best (zero it first); lowest index wins ties
 cudaError_t op_argmax(const float* logits, int n, unsigned long long* best, cudaStream_t st);
 // embedding gather: out[t] = bf16->f32(E[tokens[t]])

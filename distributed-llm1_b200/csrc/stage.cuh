@@ -54,6 +54,18 @@ struct StageParams {
   int pref_bytes;            // per-CTA L2 prefetch budget for the next phase
   unsigned long long* trace; // optional: %globaltimer (ns) at kernel start and after every barrier
   int trace_cap;
+  // Pipeline hop over NVLink peer memory (all optional). The pass first waits
+  // (bounded) until *in_flag >= in_expect, the previous stage's signal that this
+  // pass's input rows (or, on the first stage, tokens) have landed in local
+  // memory. At the end it stores its output rows h (or, with a LM head, its
+  // tokens) straight into the next stage's receive buffer in that GPU's memory
+  // and then releases *out_flag = out_value there.
+  const unsigned int* in_flag;
+  unsigned int in_expect;
+  float* out_h;              // peer [m_rows][D]
+  int32_t* out_tok;          // peer [m_rows]
+  unsigned int* out_flag;    // peer
+  unsigned int out_value;
   float* dpart;              // split-K MLP: [grid][D] down_proj partials (one row)
   int splitk;                // use the split-K MLP (set by the host for one-row passes)
   int xs_floats;             // dynamic smem partition

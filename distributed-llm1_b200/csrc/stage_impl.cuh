@@ -28,6 +28,9 @@ __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P)
   };
   trace();
 
+  // Pipeline hop: wait (bounded) for the previous stage's rows or tokens.
+  if (P.in_flag && !wait_peer_flag(P.in_flag, P.in_expect, P.err)) return;
+
   // Weights never depend on earlier phases: warm L2 for the first matvec.
   if (P.n_layers > 0) {
     const LayerW L0 = P.layers[0];
@@ -78,7 +81,7 @@ __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P)
     // ---- o_proj + residual (pipeline.js:66-67)
     gemv_phase<EpiResidual, M>(eo, GemvIn{P.att, QD, P.m_rows, nullptr, 0.f}, D, sm, cta, ncta, ns);
     const EpiSiluGate eg{L.wg, L.wu, P.mid, P.I};
-    prefetch_phase(eg, D, P.I, cta, ncta, P.pref_bytes);
+    prefetch_phase(eg, D, P.I, cta, ncta, P.pref_bytes, M == 1 && P.splitk ? 8 : 1);  // the MLP's unit ranges
     if (!grid_barrier(P.bar_count, P.err)) return;
     trace();
 
@@ -133,6 +136,22 @@ __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P)
     trace();
   }
 
+  if (P.out_h) {
+    // ---- hop (pipeline.js:226-253): this CTA's share of the output rows straight
+    // into the next stage's receive buffer over NVLink, then one release of its flag
+    const int n4 = (P.m_rows * D) >> 2;
+    const int v0 = (int)(((long long)cta * n4) / ncta), v1 = (int)(((long long)(cta + 1) * n4) / ncta);
+    const float4* src = reinterpret_cast<const float4*>(P.h);
+    float4* dst = reinterpret_cast<float4*>(P.out_h);
+    for (int i = v0 + threadIdx.x; i < v1; i += blockDim.x) dst[i] = __ldcg(src + i);
+    __threadfence_system();
+    if (!grid_barrier(P.bar_count, P.err)) return;
+    if (cta == 0 && threadIdx.x == 0) {
+      __threadfence_system();
+      st_release_sys_u32(P.out_flag, P.out_value);
+    }
+  }
+
   if (P.lm_head) {
     // ---- sampleLast: rmsnorm(model.norm) -> LM head -> argmax (pipeline.js:147-169)
     float* logits = nullptr;
@@ -168,9 +187,12 @@ __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P)
           P.rows[m].pos += 1;
           P.rows[m].slot += 1;
         }
+        if (P.out_tok) P.out_tok[m] = tok;  // the tokens go back to the first stage
       }
+      if (P.out_tok) __threadfence_system();
       __syncthreads();
       if (threadIdx.x == 0 && P.step_count) atomicAdd(P.step_count, 1);
+      if (threadIdx.x == 0 && P.out_tok) st_release_sys_u32(P.out_flag, P.out_value);
     }
   } else if (P.advance_rows && cta == 0 && threadIdx.x < P.m_rows) {
     P.rows[threadIdx.x].pos += 1;

@@ -88,6 +88,10 @@ class KernelContext:
         """Enqueue on a caller-owned cudaStream_t (e.g. torch.cuda.current_stream().cuda_stream)."""
         self._check(self.lib.dllm_ctx_set_stream(self.handle, cuda_stream or None), "set_stream")
 
+    def set_tensor_core_rows(self, min_rows: int):
+        """Passes of >= min_rows rows use the tcgen05 GEMM (0: never); default 16."""
+        self._check(self.lib.dllm_ctx_set_tensor_core_rows(self.handle, int(min_rows)), "set_tensor_core_rows")
+
     def synchronize(self, timeout_ms: int = 15000):
         self._check(self.lib.dllm_ctx_synchronize(self.handle, timeout_ms), "synchronize")
 

@@ -90,6 +90,11 @@ int dllm_ctx_set_stream(dllm_ctx* ctx, void* cuda_stream);
 int dllm_ctx_synchronize(dllm_ctx* ctx, int timeout_ms);
 /* Number of kernels this ctx has launched (host counter, for launch accounting). */
 uint64_t dllm_ctx_launch_count(const dllm_ctx* ctx);
+/* Passes of at least `min_rows` rows (MATMUL with n > 1, kernels.js:26-44; prefill
+ * chunks and wide micro-batches of Stage.forward, pipeline.js:48-78) run their
+ * projections as tcgen05 tensor-core GEMMs; fewer rows use the CUDA-core matvec.
+ * Default 16; 0 keeps every pass on the matvec; otherwise 2..128. */
+int dllm_ctx_set_tensor_core_rows(dllm_ctx* ctx, int min_rows);
 
 /* ---- buffers (kernels.js:181-211) ----------------------------------------- */
 /* ctx.loadWeightBits(u32arr, label) (kernels.js:181-186): one u32 per bf16
@@ -224,6 +229,43 @@ int dllm_leader_set_keep_logits(dllm_leader* ld, int keep);
 int dllm_leader_last_logits(dllm_leader* ld, float* out);
 /* Logits of kept step `index` (0 = the prefill's sample) of the latest call. */
 int dllm_leader_read_logits(dllm_leader* ld, int index, float* out);
+
+/* ---- multi-GPU pipeline (pipeline.js:6-87 layer-range stages, :91-282 leader loop) ----
+ * One process (or thread) per GPU holds one Stage of a contiguous layer range
+ * (assignLayers, pipeline.js:6-23); rank 0's stage also embeds tokens, the last
+ * rank's stage holds the final norm and LM head. n_micro micro-batches of
+ * `micro` sequences (sequence ids b*micro .. (b+1)*micro-1 of every stage's KV
+ * cache) circulate the ring rank 0 -> 1 -> ... -> last -> 0, so with n_micro >=
+ * world every GPU works on some micro-batch at once. The hidden-row hop of the
+ * reference (frames over WebRTC, pipeline.js:226-253) is fused into the stage
+ * kernel: a pass ends by storing its rows (the last stage: its greedy tokens) in
+ * the next GPU's receive buffer over NVLink and releasing a flag there; the next
+ * pass starts with a bounded wait on its flag. No host round trip per hop.
+ * Set-up: every rank creates its pipeline, publishes dllm_pipeline_handle
+ * (a CUDA IPC handle of its receive buffer) over the host's own channel, and
+ * connects to the handle of rank (rank + 1) % world. Before the first run all
+ * ranks should be connected (a host barrier), since a pass waits for its input
+ * at most a few seconds. */
+typedef struct dllm_pipeline dllm_pipeline;
+#define DLLM_PIPELINE_HANDLE_BYTES 64
+/* micro <= 8; n_micro * micro <= the stage's max_seqs. Row i of micro-batch b is
+ * sequence b*micro + i at its current T0 (position == slot == T0). */
+int dllm_pipeline_create(dllm_stage* st, int rank, int world, int n_micro, int micro, dllm_pipeline** out);
+void dllm_pipeline_destroy(dllm_pipeline* pl);
+/* This rank's receive buffer as DLLM_PIPELINE_HANDLE_BYTES opaque bytes. */
+int dllm_pipeline_handle(const dllm_pipeline* pl, uint8_t* handle_out);
+/* Map the receive buffer of rank (rank + 1) % world (its dllm_pipeline_handle). */
+int dllm_pipeline_connect(dllm_pipeline* pl, const uint8_t* next_rank_handle);
+/* Rank 0: the first token of every sequence (n_micro * micro, in sequence order). */
+int dllm_pipeline_set_tokens(dllm_pipeline* pl, const int32_t* tokens, int n);
+/* Enqueue `steps` greedy decode steps of every micro-batch (steps * n_micro
+ * passes on this rank, in ring order) on the stage ctx's stream; no host wait. */
+int dllm_pipeline_run(dllm_pipeline* pl, int steps);
+/* Last rank: the tokens sampled by the latest run, [steps][n_micro * micro]
+ * (bounded wait; a pass whose input never arrived reports DLLM_ETIMEOUT). */
+int dllm_pipeline_read_tokens(dllm_pipeline* pl, int32_t* out, int steps);
+/* Bounded wait for this rank's enqueued passes, then its device error flag. */
+int dllm_pipeline_synchronize(dllm_pipeline* pl, int timeout_ms);
 
 /* ---- attention that allocates nothing ---------------------------------------
  * No counterpart in the reference. For callers that must not allocate device
