@@ -53,6 +53,9 @@ def parse_args():
     p.add_argument("--micro", type=int, default=1, help="sequences per micro-batch (N>1)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-steps", type=int, default=3, help="tokens in the CPU baseline sample")
+    p.add_argument("--kernel-sweep", action="store_true",
+                   help="isolated kernel sweep (matvec / tensor-core GEMM shapes, attention lengths, RMSNorm and "
+                        "RoPE at hidden 3584): one JSON line per case instead of the decode benchmark")
     p.add_argument("--layers", type=int, default=0,
                    help="profiling case only: run the first N layers + LM head (a few GB on the device); "
                         "the line is marked and is not the benchmark")
@@ -341,8 +344,95 @@ def run_single(args):
     return res
 
 
+# ---- isolated kernel sweep ------------------------------------------------------------------
+SWEEP_SHAPES = [(896, 1152), (1536, 8960), (3584, 18944), (18944, 3584), (3584, 152064)]
+SWEEP_ATTN = [1024, 4096, 16384, 32768]
+
+
+def run_kernel_sweep(args):
+    """CUDA-event time per launch of each kernel in isolation, with an L2 flush
+    (a 512 MB write) before every timed launch, and its fraction of the measured
+    HBM copy peak: matvec (one row; the stage kernel's matvec phase as an op) and
+    the tcgen05 GEMM (16 and 64 rows) at the sweep shapes, decode attention over
+    1k-32k slots (28 Q / 4 KV heads, head_dim 128; the reference's fp32 cache
+    layout), and RMSNorm + RoPE of one row at hidden 3584."""
+    import numpy as np
+    import torch
+    dllm = importlib.import_module("distributed-llm1_b200")
+    torch.cuda.set_device(0)
+    stream = torch.cuda.current_stream()
+    peak, peak_kind = measured_peaks()
+    flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    lines = []
+
+    def timed(fn, iters=20, warm=3):
+        for _ in range(warm):
+            fn()
+        ts = []
+        for _ in range(iters):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1) * 1e-3)
+        return float(np.median(ts))
+
+    def emit(kernel, shape, sec, nbytes, flops=None, launches=1):
+        d = {"sweep": kernel, "shape": shape, "us": sec * 1e6, "bytes": nbytes, "gbs": nbytes / sec / 1e9,
+             "hbm_frac": nbytes / sec / 1e9 / peak, "peak_gbs": peak, "peak_kind": peak_kind,
+             "kernel_launches": launches}
+        if flops:
+            d["tflops"] = flops / sec / 1e12
+        print(json.dumps(d), flush=True)
+        lines.append(d)
+
+    cfg = dllm.PRESETS["qwen2.5-7b"].with_(num_layers=1, kv_dtype="f32", max_pos=max(SWEEP_ATTN) + 8)
+    ctx = dllm.initKernels(0, cfg)
+    ctx.set_stream(stream.cuda_stream)
+    rng = np.random.default_rng(0)
+    for K, N in SWEEP_SHAPES:
+        w = ctx.createBf16(K * N, "w")
+        ctx.fillNormalBf16(w, K + N, WEIGHT_STD)
+        for n in (1, 16, 64):
+            x = ctx.createF32(n * K, "x")
+            ctx.writeF32(x, rng.standard_normal(n * K).astype(np.float32))
+            # the output buffer is dropped at once and comes back from the ctx's buffer cache
+            sec = timed(lambda: ctx.matmul(x, w, n, K, N))
+            nbytes = 2 * K * N + 4 * n * (K + N)
+            emit("matvec (CUDA cores)" if n == 1 else "GEMM (tcgen05, hi+lo bf16 activations)",
+                 f"n={n} [K={K},N={N}]", sec, nbytes, flops=2.0 * n * K * N, launches=1 if n == 1 else 2)
+        del w
+    QD, KD = cfg.num_q_heads * cfg.head_dim, cfg.num_kv_heads * cfg.head_dim
+    kc = ctx.createF32(cfg.max_pos * KD, "k")
+    vc = ctx.createF32(cfg.max_pos * KD, "v")
+    ctx.writeF32(kc, rng.standard_normal(cfg.max_pos * KD).astype(np.float32))
+    ctx.writeF32(vc, rng.standard_normal(cfg.max_pos * KD).astype(np.float32))
+    q = ctx.createF32(QD, "q")
+    ctx.writeF32(q, rng.standard_normal(QD).astype(np.float32))
+    for T in SWEEP_ATTN:
+        sec = timed(lambda: ctx.attention(q, kc, vc, T - 1, 1))
+        emit("decode attention (fp32 cache, reference layout)", f"T={T} 28/4 heads hd=128", sec,
+             2 * T * KD * 4 + 2 * QD * 4)
+    D = cfg.hidden_size
+    h = ctx.createF32(D, "h")
+    ctx.writeF32(h, rng.standard_normal(D).astype(np.float32))
+    g = ctx.createBf16(D, "g")
+    ctx.fillConstBf16(g, 1.0)
+    sec = timed(lambda: ctx.rmsnorm(h, g, 1))
+    emit("rmsnorm", "1 row, hidden 3584", sec, D * 4 * 2 + D * 2)
+    sec = timed(lambda: ctx.ropeQ(q, 2048, 1))
+    emit("rope (q, 28 heads)", "1 row, theta 1e6", sec, QD * 4 * 2)
+    ctx.close()
+    return lines
+
+
 def main():
     args = parse_args()
+    if args.kernel_sweep:
+        run_kernel_sweep(args)
+        return
     if args.impl == "reference":
         res = run_reference(args)
     elif args.gpus <= 1:

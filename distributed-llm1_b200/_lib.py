@@ -122,6 +122,8 @@ SIGNATURES = {
     "dllm_pipeline_run": (C.c_int, [P, C.c_int]),
     "dllm_pipeline_read_tokens": (C.c_int, [P, I32P, C.c_int]),
     "dllm_pipeline_synchronize": (C.c_int, [P, C.c_int]),
+    "dllm_pipeline_set_host_tokens": (C.c_int, [P, C.c_int]),
+    "dllm_pipeline_run_micro": (C.c_int, [P, C.c_int, I32P, I32P]),
     "dllm_attention_noalloc": (C.c_int, [P, P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, P]),
     "dllm_attention_noalloc_status": (C.c_int, [P, C.c_int, I32P]),
 }

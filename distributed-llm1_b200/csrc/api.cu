@@ -75,6 +75,9 @@ struct dllm_ctx {
   int tc_min_rows = dllm::kTcMinRows;
   void* tc_scratch = nullptr;
   size_t tc_scratch_bytes = 0;
+  // freed buffers kept for reuse, by size in bytes
+  std::multimap<size_t, void*> buf_cache;
+  size_t buf_cache_bytes = 0;
 };
 
 struct dllm_stage {
@@ -242,7 +245,25 @@ int check_bf16(dllm_ctx* c, const dllm_buf* b, size_t need, const char* what) {
   return DLLM_OK;
 }
 
-int new_buf(dllm_ctx* c, size_t n, int dtype, const char* label, dllm_buf** out) {
+// Buffers of a ctx come from, and return to, a per-ctx cache of freed device
+// blocks keyed by size: the op outputs of a forward (one per op, as the reference
+// creates them, kernels.js:222-301) then cost no cudaMalloc/cudaFree (which can
+// synchronise the device) after the first pass. Reuse is safe because every op
+// of a ctx runs on its one stream, in order.
+constexpr size_t kBufCacheBytes = (size_t)4 << 30;
+
+void* cache_take(dllm_ctx* c, size_t bytes) {
+  auto it = c->buf_cache.find(bytes);
+  if (it == c->buf_cache.end()) return nullptr;
+  void* p = it->second;
+  c->buf_cache.erase(it);
+  c->buf_cache_bytes -= bytes;
+  return p;
+}
+
+// zero: fill with zeros (createF32 semantics); op outputs that the kernel fully
+// overwrites skip it.
+int new_buf(dllm_ctx* c, size_t n, int dtype, const char* label, dllm_buf** out, bool zero = true) {
   auto* b = new dllm_buf();
   b->ctx = c;
   b->device = c->device;
@@ -250,18 +271,23 @@ int new_buf(dllm_ctx* c, size_t n, int dtype, const char* label, dllm_buf** out)
   b->dtype = dtype;
   b->bytes = n * (dtype == 0 ? 4 : 2);
   b->label = label ? label : "";
-  cudaError_t e = cudaMalloc(&b->ptr, b->bytes);
-  if (e != cudaSuccess) {
-    cudaGetLastError();
-    delete b;
-    return set_err(c, DLLM_ENOMEM, "cudaMalloc(%zu bytes, %s): %s", n * (dtype == 0 ? 4 : 2), label ? label : "",
-                   cudaGetErrorString(e));
+  b->ptr = cache_take(c, b->bytes);
+  if (!b->ptr) {
+    cudaError_t e = cudaMalloc(&b->ptr, b->bytes);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      delete b;
+      return set_err(c, DLLM_ENOMEM, "cudaMalloc(%zu bytes, %s): %s", n * (dtype == 0 ? 4 : 2), label ? label : "",
+                     cudaGetErrorString(e));
+    }
   }
-  e = cudaMemsetAsync(b->ptr, 0, b->bytes, c->stream);
-  if (e != cudaSuccess) {
-    cudaFree(b->ptr);
-    delete b;
-    return set_err(c, DLLM_ECUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+  if (zero) {
+    cudaError_t e = cudaMemsetAsync(b->ptr, 0, b->bytes, c->stream);
+    if (e != cudaSuccess) {
+      cudaFree(b->ptr);
+      delete b;
+      return set_err(c, DLLM_ECUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+    }
   }
   ctx_retain(c);
   *out = b;
@@ -688,6 +714,8 @@ void ctx_free(dllm_ctx* c) {
   dev_free(c->attn.arrive);
   dev_free(c->attn_rows);
   dev_free(c->tc_scratch);
+  for (auto& kv : c->buf_cache) cudaFree(kv.second);
+  c->buf_cache.clear();
   if (c->err_host) cudaFreeHost(c->err_host);
   if (c->best_host) cudaFreeHost(c->best_host);
   if (c->sync_event) cudaEventDestroy(c->sync_event);
@@ -899,9 +927,16 @@ int dllm_read_bf16(dllm_ctx* c, const dllm_buf* b, uint16_t* dst, size_t n) {
 void dllm_buf_free(dllm_buf* b) {
   if (!b) return;
   if (--b->refs > 0) return;
-  cudaSetDevice(b->device);
-  if (b->ptr) cudaFree(b->ptr);
   dllm_ctx* c = b->ctx;
+  if (b->ptr) {
+    if (c && c->buf_cache_bytes + b->bytes <= kBufCacheBytes) {
+      c->buf_cache.emplace(b->bytes, b->ptr);  // reused by the next buffer of this size
+      c->buf_cache_bytes += b->bytes;
+    } else {
+      cudaSetDevice(b->device);
+      cudaFree(b->ptr);
+    }
+  }
   delete b;
   ctx_release(c);
 }
@@ -937,7 +972,7 @@ int dllm_matmul(dllm_ctx* c, const dllm_buf* x, const dllm_buf* w, int n, int di
   if (int rc = check_bf16(c, w, (size_t)din * dout, "matmul w")) return rc;
   if (int rc = use_device(c)) return rc;
   dllm_buf* o = nullptr;
-  if (int rc = new_buf(c, (size_t)n * dout, 0, "mm_out", &o)) return rc;
+  if (int rc = new_buf(c, (size_t)n * dout, 0, "mm_out", &o, false)) return rc;
   if (c->tc_min_rows > 0 && n >= c->tc_min_rows) {
     // a real GEMM: the tcgen05 path
     if (int rc = tc_rows(c, (const float*)x->ptr, n, din, (const __nv_bfloat16*)w->ptr, dout, (float*)o->ptr, 0,
@@ -968,7 +1003,7 @@ int dllm_rmsnorm(dllm_ctx* c, const dllm_buf* x, const dllm_buf* g, int n, dllm_
   if (int rc = check_bf16(c, g, (size_t)D, "rmsnorm g")) return rc;
   if (int rc = use_device(c)) return rc;
   dllm_buf* o = nullptr;
-  if (int rc = new_buf(c, (size_t)n * D, 0, "rms_out", &o)) return rc;
+  if (int rc = new_buf(c, (size_t)n * D, 0, "rms_out", &o, false)) return rc;
   cudaError_t e = dllm::op_rmsnorm((const float*)x->ptr, (const __nv_bfloat16*)g->ptr, (float*)o->ptr, n, D,
                                    c->cfg.rms_norm_eps, c->stream);
   if (e != cudaSuccess) {
@@ -1037,7 +1072,7 @@ int dllm_attention(dllm_ctx* c, const dllm_buf* q, const dllm_buf* kcache, const
   int ms = c->sms / (std::max(1, std::min(n, 8)) * f.num_kv_heads);
   c->attn.max_splits = std::max(1, std::min(ms, kMaxSplitsAlloc));
   dllm_buf* o = nullptr;
-  if (int rc = new_buf(c, (size_t)n * QD, 0, "attn_out", &o)) return rc;
+  if (int rc = new_buf(c, (size_t)n * QD, 0, "attn_out", &o, false)) return rc;
   cudaError_t e = dllm::op_attention((const float*)q->ptr, (const float*)kcache->ptr, (const float*)vcache->ptr,
                                      (float*)o->ptr, c->attn_rows, n, f.num_q_heads, f.num_kv_heads, f.head_dim,
                                      max_pos, c->scale, c->attn, c->err_dev, c->sms, c->stream);
@@ -1058,7 +1093,7 @@ int dllm_silu_mul(dllm_ctx* c, const dllm_buf* a, const dllm_buf* b, int total, 
   if (int rc = check_f32(c, b, total, "siluMul b")) return rc;
   if (int rc = use_device(c)) return rc;
   dllm_buf* o = nullptr;
-  if (int rc = new_buf(c, total, 0, "silu_out", &o)) return rc;
+  if (int rc = new_buf(c, total, 0, "silu_out", &o, false)) return rc;
   CK(c, dllm::op_silu_mul((const float*)a->ptr, (const float*)b->ptr, (float*)o->ptr, total, c->stream));
   c->launches += 1;
   *out = o;
@@ -1073,7 +1108,7 @@ int dllm_add(dllm_ctx* c, const dllm_buf* a, const dllm_buf* b, int n, dllm_buf*
   if (int rc = check_f32(c, b, n, "add b")) return rc;
   if (int rc = use_device(c)) return rc;
   dllm_buf* o = nullptr;
-  if (int rc = new_buf(c, n, 0, "add_out", &o)) return rc;
+  if (int rc = new_buf(c, n, 0, "add_out", &o, false)) return rc;
   CK(c, dllm::op_add((const float*)a->ptr, (const float*)b->ptr, (float*)o->ptr, n, c->stream));
   c->launches += 1;
   *out = o;
@@ -1090,7 +1125,7 @@ int dllm_add_bias(dllm_ctx* c, const dllm_buf* a, const dllm_buf* bias, int n, i
   if (int rc = check_bf16(c, bias, dout, "addBias bias")) return rc;
   if (int rc = use_device(c)) return rc;
   dllm_buf* o = nullptr;
-  if (int rc = new_buf(c, (size_t)total, 0, "bias_out", &o)) return rc;
+  if (int rc = new_buf(c, (size_t)total, 0, "bias_out", &o, false)) return rc;
   CK(c, dllm::op_add_bias((const float*)a->ptr, (const __nv_bfloat16*)bias->ptr, (float*)o->ptr, (int)total, dout,
                           c->stream));
   c->launches += 1;
@@ -1267,7 +1302,7 @@ int dllm_stage_forward(dllm_stage* s, const float* hidden, int n, int pos_start,
   }
   s->T0[0] += n;  // pipeline.js:76
   dllm_buf* o = nullptr;
-  if (int rc = new_buf(c, (size_t)n * D, 0, "stage_out", &o)) return rc;
+  if (int rc = new_buf(c, (size_t)n * D, 0, "stage_out", &o, false)) return rc;
   CK(c, cudaMemcpyAsync(o->ptr, s->hbuf, (size_t)n * D * 4, cudaMemcpyDeviceToDevice, c->stream));
   *out = o;
   return DLLM_OK;
@@ -1788,6 +1823,7 @@ struct dllm_pipeline {
   int hist_cap = 0, hist_steps = 0;
   std::vector<unsigned int> passes;  // passes run per micro-batch
   bool connected = false;
+  bool host_tokens = false;  // the first stage takes tokens from the host, not from the last stage
 };
 
 namespace {
@@ -1914,73 +1950,116 @@ int dllm_pipeline_set_tokens(dllm_pipeline* pl, const int32_t* tokens, int n) {
   return sync_check(c, kDefaultTimeoutMs);
 }
 
+namespace {
+// One pass of micro-batch b on this rank (enqueued). `hist_row`: where the last
+// stage keeps the sampled tokens (device), or null.
+int pipeline_pass(dllm_pipeline* pl, int b, int32_t* hist_row) {
+  dllm_ctx* c = pl->ctx;
+  dllm_stage* s = pl->st;
+  const int m = pl->micro, D = c->cfg.hidden_size;
+  const bool first = pl->rank == 0, last = pl->rank == pl->world - 1;
+  for (int i = 0; i < m; ++i)
+    if (s->T0[b * m + i] + 1 > s->max_slots)
+      return set_err(c, DLLM_ERANGE, "KV cache overflow: seq %d T0=%d maxPos=%d", b * m + i, s->T0[b * m + i],
+                     s->max_slots);
+  const unsigned int k = pl->passes[b];  // passes of b so far on this rank
+  StageParams P = base_params(s);
+  P.m_rows = m;
+  P.rows = pl->rows + (size_t)b * m;
+  P.advance_rows = 1;
+  if (first) {
+    P.h = pl->h0 + (size_t)b * m * D;
+    P.tokens_in = rx_tok(pl, pl->rx, b);
+    if (k > 0 && pl->world > 1 && !pl->host_tokens) {  // the previous round's tokens, from the last stage
+      P.in_flag = rx_flag(pl, pl->rx, b);
+      P.in_expect = k;
+    }
+  } else {
+    P.h = rx_h(pl, pl->rx, b);
+    P.in_flag = rx_flag(pl, pl->rx, b);
+    P.in_expect = k + 1;
+  }
+  if (last) {
+    P.lm_head = s->lm_head;
+    P.tokens_out = pl->world == 1 ? rx_tok(pl, pl->rx, b) : pl->tok_out + (size_t)b * m;
+    if (pl->world > 1 && !pl->host_tokens) {
+      P.out_tok = rx_tok(pl, pl->peer_rx, b);
+      P.out_flag = rx_flag(pl, pl->peer_rx, b);
+      P.out_value = k + 1;
+    }
+  } else {
+    P.lm_head = nullptr;
+    P.out_h = rx_h(pl, pl->peer_rx, b);
+    P.out_flag = rx_flag(pl, pl->peer_rx, b);
+    P.out_value = k + 1;
+  }
+  if (int rc = launch(s, P)) return rc;
+  if (last && hist_row)
+    CK(c, cudaMemcpyAsync(hist_row, P.tokens_out, (size_t)m * 4, cudaMemcpyDeviceToDevice, c->stream));
+  pl->passes[b] = k + 1;
+  for (int i = 0; i < m; ++i) s->T0[b * m + i] += 1;
+  return DLLM_OK;
+}
+
+int pipeline_ready(dllm_pipeline* pl) {
+  dllm_ctx* c = pl->ctx;
+  if (!pl->connected) return set_err(c, DLLM_EINVAL, "pipeline: not connected to the next stage");
+  if (int rc = use_device(c)) return rc;
+  return resolve(pl->st);
+}
+}  // namespace
+
 int dllm_pipeline_run(dllm_pipeline* pl, int steps) {
   if (!pl) return DLLM_EINVAL;
   dllm_ctx* c = pl->ctx;
-  dllm_stage* s = pl->st;
   if (steps < 1) return set_err(c, DLLM_EINVAL, "pipeline_run: invalid steps=%d", steps);
-  if (!pl->connected) return set_err(c, DLLM_EINVAL, "pipeline_run: not connected to the next stage");
-  const int B = pl->n_micro, m = pl->micro, D = c->cfg.hidden_size;
-  for (int q = 0; q < B * m; ++q)
-    if (s->T0[q] + steps > s->max_slots)
-      return set_err(c, DLLM_ERANGE, "KV cache overflow: seq %d T0=%d + %d steps > maxPos=%d", q, s->T0[q], steps,
-                     s->max_slots);
-  if (int rc = use_device(c)) return rc;
-  if (int rc = resolve(s)) return rc;
-  const bool first = pl->rank == 0, last = pl->rank == pl->world - 1;
-  if (last) {
-    if (steps > pl->hist_cap) {
-      CK(c, cudaStreamSynchronize(c->stream));
-      dev_free(pl->hist);
-      pl->hist = nullptr;
-      pl->hist_cap = 0;
-      if (int rc = dev_alloc(c, &pl->hist, (size_t)steps * B * m, "pipeline token history")) return rc;
-      pl->hist_cap = steps;
-    }
+  if (int rc = pipeline_ready(pl)) return rc;
+  const int B = pl->n_micro, m = pl->micro;
+  const bool last = pl->rank == pl->world - 1;
+  if (last && steps > pl->hist_cap) {
+    CK(c, cudaStreamSynchronize(c->stream));
+    dev_free(pl->hist);
+    pl->hist = nullptr;
+    pl->hist_cap = 0;
+    if (int rc = dev_alloc(c, &pl->hist, (size_t)steps * B * m, "pipeline token history")) return rc;
+    pl->hist_cap = steps;
   }
-  for (int step = 0; step < steps; ++step) {
-    for (int b = 0; b < B; ++b) {
-      const unsigned int k = pl->passes[b];  // passes of b so far on this rank
-      StageParams P = base_params(s);
-      P.m_rows = m;
-      P.rows = pl->rows + (size_t)b * m;
-      P.advance_rows = 1;
-      if (first) {
-        P.h = pl->h0 + (size_t)b * m * D;
-        P.tokens_in = rx_tok(pl, pl->rx, b);
-        if (k > 0 && pl->world > 1) {  // tokens of the previous round, from the last stage
-          P.in_flag = rx_flag(pl, pl->rx, b);
-          P.in_expect = k;
-        }
-      } else {
-        P.h = rx_h(pl, pl->rx, b);
-        P.in_flag = rx_flag(pl, pl->rx, b);
-        P.in_expect = k + 1;
-      }
-      if (last) {
-        P.lm_head = s->lm_head;
-        P.tokens_out = pl->world == 1 ? rx_tok(pl, pl->rx, b) : pl->tok_out + (size_t)b * m;
-        if (pl->world > 1) {
-          P.out_tok = rx_tok(pl, pl->peer_rx, b);
-          P.out_flag = rx_flag(pl, pl->peer_rx, b);
-          P.out_value = k + 1;
-        }
-      } else {
-        P.lm_head = nullptr;
-        P.out_h = rx_h(pl, pl->peer_rx, b);
-        P.out_flag = rx_flag(pl, pl->peer_rx, b);
-        P.out_value = k + 1;
-      }
-      if (int rc = launch(s, P)) return rc;
-      if (last)
-        CK(c, cudaMemcpyAsync(pl->hist + ((size_t)step * B + b) * m, P.tokens_out, (size_t)m * 4,
-                              cudaMemcpyDeviceToDevice, c->stream));
-      pl->passes[b] = k + 1;
-      for (int i = 0; i < m; ++i) s->T0[b * m + i] += 1;
-    }
-  }
+  for (int step = 0; step < steps; ++step)
+    for (int b = 0; b < B; ++b)
+      if (int rc = pipeline_pass(pl, b, last ? pl->hist + ((size_t)step * B + b) * m : nullptr)) return rc;
   pl->hist_steps = last ? steps : 0;
   return DLLM_OK;
+}
+
+int dllm_pipeline_set_host_tokens(dllm_pipeline* pl, int on) {
+  if (!pl) return DLLM_EINVAL;
+  if (int rc = use_device(pl->ctx)) return rc;
+  CK(pl->ctx, cudaStreamSynchronize(pl->ctx->stream));
+  pl->host_tokens = on != 0;
+  return DLLM_OK;
+}
+
+int dllm_pipeline_run_micro(dllm_pipeline* pl, int b, const int32_t* tokens, int32_t* tokens_out) {
+  if (!pl) return DLLM_EINVAL;
+  dllm_ctx* c = pl->ctx;
+  const int m = pl->micro;
+  if (b < 0 || b >= pl->n_micro) return set_err(c, DLLM_EINVAL, "pipeline_run_micro: invalid micro-batch %d", b);
+  const bool first = pl->rank == 0, last = pl->rank == pl->world - 1;
+  if (first && pl->host_tokens && !tokens)
+    return set_err(c, DLLM_EINVAL, "pipeline_run_micro: the first stage needs the micro-batch's tokens");
+  if (last && !tokens_out) return set_err(c, DLLM_EINVAL, "pipeline_run_micro: the last stage returns tokens");
+  if (int rc = pipeline_ready(pl)) return rc;
+  if (first && tokens) {
+    for (int i = 0; i < m; ++i)
+      if (tokens[i] < 0 || tokens[i] >= c->cfg.vocab_size)
+        return set_err(c, DLLM_EINVAL, "pipeline_run_micro: token %d out of range", tokens[i]);
+    CK(c, cudaMemcpyAsync(rx_tok(pl, pl->rx, b), tokens, (size_t)m * 4, cudaMemcpyHostToDevice, c->stream));
+  }
+  if (int rc = pipeline_pass(pl, b, nullptr)) return rc;
+  if (!last) return DLLM_OK;
+  const int32_t* src = pl->world == 1 ? rx_tok(pl, pl->rx, b) : pl->tok_out + (size_t)b * m;
+  CK(c, cudaMemcpyAsync(tokens_out, src, (size_t)m * 4, cudaMemcpyDeviceToHost, c->stream));
+  return sync_check(c, kDefaultTimeoutMs);
 }
 
 int dllm_pipeline_read_tokens(dllm_pipeline* pl, int32_t* out, int steps) {

@@ -118,6 +118,92 @@ class StageCompute:
                                 tok_out.data_ptr() if tok_out is not None else None)
 
 
+class NvlinkRing:
+    """The C-ABI pipeline (dllm_pipeline_*): this rank's Stage in a ring of
+    stages whose hidden-row hop is fused into the stage kernel (rows stored in
+    the next GPU's receive buffer over NVLink, a flag released there). The host
+    only exchanges the receive buffers' IPC handles once (`connect_ring`)."""
+
+    def __init__(self, stage, rank: int, world: int, n_micro: int, micro: int):
+        import ctypes as C
+        from . import _lib
+        self.C, self._lib = C, _lib
+        self.stage, self.lib = stage, stage.lib
+        self.rank, self.world, self.n_micro, self.micro = rank, world, n_micro, micro
+        h = C.c_void_p()
+        stage.k._check(self.lib.dllm_pipeline_create(stage.handle, rank, world, n_micro, micro, C.byref(h)),
+                       "pipeline_create")
+        self.handle = h.value
+
+    def _check(self, st, what):
+        self.stage.k._check(st, what)
+
+    def ipc_handle(self) -> bytes:
+        C = self.C
+        buf = (C.c_uint8 * 64)()
+        self._check(self.lib.dllm_pipeline_handle(self.handle, buf), "pipeline_handle")
+        return bytes(buf)
+
+    def connect(self, next_handle: bytes):
+        C = self.C
+        buf = (C.c_uint8 * 64).from_buffer_copy(next_handle)
+        self._check(self.lib.dllm_pipeline_connect(self.handle, buf), "pipeline_connect")
+
+    def set_tokens(self, tokens):
+        import numpy as np
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        self._check(self.lib.dllm_pipeline_set_tokens(self.handle, self._lib.ptr(t, self.C.c_int32), t.size),
+                    "pipeline_set_tokens")
+
+    def run(self, steps: int):
+        self._check(self.lib.dllm_pipeline_run(self.handle, steps), "pipeline_run")
+
+    def read_tokens(self, steps: int):
+        import numpy as np
+        out = np.zeros((steps, self.n_micro * self.micro), np.int32)
+        self._check(self.lib.dllm_pipeline_read_tokens(self.handle, self._lib.ptr(out, self.C.c_int32), steps),
+                    "pipeline_read_tokens")
+        return out
+
+    def synchronize(self, timeout_ms: int = 15000):
+        self._check(self.lib.dllm_pipeline_synchronize(self.handle, timeout_ms), "pipeline_synchronize")
+
+    def set_host_tokens(self, on: bool):
+        self._check(self.lib.dllm_pipeline_set_host_tokens(self.handle, int(bool(on))), "pipeline_set_host_tokens")
+
+    def run_micro(self, b: int, tokens=None):
+        """One pass of micro-batch b; the first stage passes host tokens (host-token
+        mode), the last stage gets the sampled tokens back."""
+        import numpy as np
+        C = self.C
+        t = None if tokens is None else np.ascontiguousarray(tokens, dtype=np.int32)
+        out = np.zeros(self.micro, np.int32) if self.rank == self.world - 1 else None
+        self._check(self.lib.dllm_pipeline_run_micro(self.handle, b, self._lib.ptr(t, C.c_int32),
+                                                     self._lib.ptr(out, C.c_int32)), "pipeline_run_micro")
+        return out
+
+    def close(self):
+        if getattr(self, "handle", None):
+            self.lib.dllm_pipeline_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def connect_ring(ring: NvlinkRing, group=None):
+    """Exchange the receive-buffer handles over torch.distributed and map the next
+    rank's buffer; ends with a barrier so no pass starts before every rank is
+    connected."""
+    handles = [None] * ring.world
+    dist.all_gather_object(handles, ring.ipc_handle(), group=group)
+    ring.connect(handles[(ring.rank + 1) % ring.world])
+    dist.barrier(group=group)
+
+
 def init_distributed(backend: str = "nccl", timeout_s: int = 120):
     """One process per GPU; rendezvous from torchrun's environment."""
     import datetime
@@ -133,54 +219,59 @@ def init_distributed(backend: str = "nccl", timeout_s: int = 120):
 
 
 def bench_pipeline(args, bench):
-    """`bench.py --gpus N` under torchrun: N stages, N micro-batches of args.micro
-    sequences, 2048-slot synthetic KV per sequence; returns rank 0's JSON dict."""
+    """`bench.py --gpus N` under torchrun: N stages (plan_stages), N micro-batches of
+    args.micro sequences, 2048-slot synthetic KV per sequence, decoded through the
+    NVLink ring of the C ABI (dllm_pipeline_*); returns rank 0's JSON dict."""
     import importlib
     import time
+    import numpy as np
     dllm = importlib.import_module("distributed-llm1_b200")
     rank, world, local = init_distributed("nccl")
     assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE {world}"
     B, m = world, args.micro
-    steps_total = args.warmup + 2 * args.steps + 4  # warm-up, timed and e2e rounds
+    e2e_steps = max(2, args.steps // 2)
+    steps_total = args.warmup + args.steps + e2e_steps + 4
     cfg = dllm.PRESETS[args.model].with_(kv_dtype="bf16", max_seqs=B * m,
                                          max_pos=args.kv_len + steps_total + 16)
-    start, end = dllm.plan_stages(cfg, world)[rank]
+    stages = dllm.plan_stages(cfg, world)
+    start, end = stages[rank]
     stream = torch.cuda.current_stream()
     ctx = dllm.initKernels(local, cfg)
     ctx.set_stream(stream.cuda_stream)
     st = dllm.Stage(ctx, start, end)
     bufs = bench.device_weights(ctx, st, cfg, start, end, embed=(rank == 0), head=(rank == world - 1))
-    for s in range(B * m):
-        st.fill_kv_random(s, args.kv_len, seed=1 + s)
+    for q in range(B * m):
+        st.fill_kv_random(q, args.kv_len, seed=1 + q)
     ctx.synchronize(300000)
-    plan = Plan(rank, world, B, m)
-    first = torch.arange(B * m, dtype=torch.int32, device="cuda") + 1000
-    runner = PipelineRunner(plan, cfg.hidden_size, torch.device("cuda", local), StageCompute(st, plan), first)
-    # create the NCCL communicator with a collective every rank joins
-    dist.all_reduce(torch.zeros(1, device="cuda"))
-    runner.run_ticks(args.warmup * B + (world - 1))  # fill the pipe, then warm up
+    ring = NvlinkRing(st, rank, world, B, m)
+    connect_ring(ring)
+    if rank == 0:
+        ring.set_tokens(np.arange(B * m, dtype=np.int32) + 1000)
+    ring.run(args.warmup)  # fills the ring, then warms up
+    ring.synchronize(120000)
     launches0 = ctx.launch_count
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     dist.barrier()
     torch.cuda.synchronize()
     with bench.ClockSampler(local) as clk:
         ev0.record(stream)
-        runner.run_ticks(args.steps * B)
+        ring.run(args.steps)
         ev1.record(stream)
         ev1.synchronize()
+    ring.synchronize(120000)
     ms = torch.tensor([ev0.elapsed_time(ev1)], device="cuda")
     dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     ms = float(ms.item())
     launches = ctx.launch_count - launches0
     tokens = args.steps * B * m
     tps = tokens / (ms / 1000.0)
-    # roofline of the slowest stage: its bytes per tick over the tick time
+    # roofline of the slowest stage: its bytes per pass over the pass time
     lw = cfg.layer_weight_bytes()
     stage_bytes = []
-    for r, (s0, s1) in enumerate(dllm.plan_stages(cfg, world)):
+    for r, (s0, s1) in enumerate(stages):
         b = bench.token_bytes(cfg, s1 - s0, head=(r == world - 1), embed=(r == 0),
                               kv_positions=args.kv_len + args.warmup + args.steps / 2)
-        # micro-batch of m rows reads the weights once and m rows of KV
+        # a micro-batch of m rows reads the weights once and m rows of KV
         kv = b - (s1 - s0) * lw - (cfg.head_weight_bytes() if r == world - 1 else 0) - (2 * cfg.hidden_size if r == 0 else 0)
         stage_bytes.append(b + (m - 1) * kv)
     tick_s = ms / 1000.0 / (args.steps * B)
@@ -189,42 +280,61 @@ def bench_pipeline(args, bench):
     # DRAM traffic of the slowest stage's launch: the ncu traffic / algorithmic
     # ratio of the profiled whole-model token applied to the stage's bytes
     traffic = bench.traffic_bytes(max(stage_bytes), args.model)
-    # e2e: the same loop with every tick's tokens copied to the host and checked
-    e2e = None
+    emitted = ring.read_tokens(args.steps) if rank == world - 1 else None
     res = None
     if rank == 0:
         res = {"metric": bench.METRIC, "value": tps, "unit": bench.UNIT, "n_gpus": world, "steps": args.steps,
                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
                "vs_baseline": None, "dtype": "bf16",
                "data": "synthetic: random-init N(0,0.02) bf16 weights (device hash), N(0,1) bf16 KV",
-               "config": bench.workload_config(args, cfg) | {"stages": dllm.plan_stages(cfg, world)},
+               "config": bench.workload_config(args, cfg) | {"stages": stages},
                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                             "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
                             "algorithmic_bytes_per_launch": max(stage_bytes),
-                            "kernel": "stage_kernel of the slowest stage (one launch per micro-batch tick)"},
-               "gpu_launches": launches, "clocks": clk.summary()}
-    # e2e through the public API: per step the last rank's tokens go device -> host
-    # and rank 0's next inputs host -> device (pinned), as a user loop would
-    runner2_tok = torch.zeros(B * m, dtype=torch.int32).pin_memory()
+                            "kernel": "stage_kernel of the slowest stage (one launch per micro-batch pass; "
+                                      "the hop to the next GPU is fused into it)"},
+               "gpu_launches": launches, "clocks": clk.summary(),
+               "hop": "fused into the stage kernel: rows stored into the next GPU's receive buffer over NVLink "
+                      "(CUDA IPC mapping) + a released flag; no NCCL kernel and no host round trip per hop"}
+    # e2e through the public API with a host-fed token loop, as the reference's
+    # leader runs it: every pass of the last stage copies its sampled tokens to
+    # the host, they travel to rank 0's host, and rank 0's next pass of that
+    # micro-batch uploads them (dllm_pipeline_run_micro)
+    gloo = dist.new_group(backend="gloo")
+    ring.set_host_tokens(True)
+    dist.barrier()
+    last = world - 1
+    cur = torch.zeros(m, dtype=torch.int32)
     dist.barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    for k in range(args.steps):
-        for _ in range(B):
-            runner.step()
-        if rank == world - 1:
-            for b in range(B):
-                runner2_tok[b * m:(b + 1) * m].copy_(runner.tok_out[b], non_blocking=True)
-        if rank == 0:
-            for b in range(B):
-                runner.tok_in[b].copy_(runner.tok_in[b].cpu().pin_memory(), non_blocking=True)
+    if rank == last and world > 1:  # the relay starts with the tokens of the timed run
+        for b in range(B):
+            dist.send(torch.from_numpy(emitted[-1, b * m:(b + 1) * m].copy()), dst=0, group=gloo)
+    for k in range(e2e_steps):
+        for b in range(B):
+            if world == 1:
+                pass
+            elif rank == 0:
+                dist.recv(cur, src=last, group=gloo)
+                ring.run_micro(b, cur.numpy())
+            elif rank == last:
+                out = ring.run_micro(b)
+                if k + 1 < e2e_steps:
+                    dist.send(torch.from_numpy(out), dst=0, group=gloo)
+            else:
+                ring.run_micro(b)
+    ring.synchronize(120000)
     torch.cuda.synchronize()
     el = torch.tensor([time.perf_counter() - t0], device="cuda")
     dist.all_reduce(el, op=dist.ReduceOp.MAX)
     if rank == 0:
-        res["e2e"] = {"value": tokens / float(el.item()), "unit": bench.UNIT, "h2d_bytes_per_step": 4 * B * m,
-                      "d2h_bytes_per_step": 4 * B * m, "api": "Stage.forward_rows + NCCL hops, host token copies"}
+        res["e2e"] = {"value": e2e_steps * B * m / float(el.item()), "unit": bench.UNIT,
+                      "h2d_bytes_per_step": 4 * B * m, "d2h_bytes_per_step": 4 * B * m,
+                      "api": "dllm_pipeline_run_micro: last stage tokens device->host, relayed to rank 0's host, "
+                             "host->device into the first stage's next pass"}
     dist.barrier()
+    ring.close()
     del bufs
     st.close()
     ctx.close()

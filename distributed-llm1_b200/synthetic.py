@@ -30,16 +30,14 @@ def device_weights(ctx, stage, cfg, start: int, end: int, embed: bool, head: boo
     final norm / LM head when asked) on the device and hand them to `stage.W`.
     Returns the leader buffers by role ("embed", "norm", "lm_head")."""
     sizes = layer_sizes(cfg)
-    k = 0
     for L in range(start, end):
-        for suf, n in sizes.items():
+        for i, (suf, n) in enumerate(sizes.items()):
             name = f"model.layers.{L}.{suf}"
             b = ctx.createBf16(n, name)
             if "layernorm" in suf:
                 ctx.fillConstBf16(b, 1.0)
-            else:
-                ctx.fillNormalBf16(b, seed * 100003 + L * 97 + k, WEIGHT_STD)
-            k += 1
+            else:  # one stream per (layer, tensor): a layer gets the same values in any stage split
+                ctx.fillNormalBf16(b, seed * 100003 + L * 97 + i, WEIGHT_STD)
             stage.W[name] = b
     V, D = cfg.vocab_size, cfg.hidden_size
     bufs = {}

@@ -266,6 +266,15 @@ int dllm_pipeline_run(dllm_pipeline* pl, int steps);
 int dllm_pipeline_read_tokens(dllm_pipeline* pl, int32_t* out, int steps);
 /* Bounded wait for this rank's enqueued passes, then its device error flag. */
 int dllm_pipeline_synchronize(dllm_pipeline* pl, int timeout_ms);
+/* Host-fed token loop (the reference's leader: sampled tokens come back to the
+ * host, pipeline.js:262-267): with `on`, the last stage keeps its tokens and the
+ * first stage takes each micro-batch's tokens from dllm_pipeline_run_micro. All
+ * ranks switch together, between passes. */
+int dllm_pipeline_set_host_tokens(dllm_pipeline* pl, int on);
+/* One pass of micro-batch b on this rank. First stage (host-token mode):
+ * `tokens` (host, micro ids) are copied in first. Last stage: the sampled tokens
+ * are copied to `tokens_out` (host) with a bounded wait. Others: enqueued only. */
+int dllm_pipeline_run_micro(dllm_pipeline* pl, int b, const int32_t* tokens, int32_t* tokens_out);
 
 /* ---- attention that allocates nothing ---------------------------------------
  * No counterpart in the reference. For callers that must not allocate device
