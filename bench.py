@@ -53,7 +53,8 @@ def parse_args():
     p.add_argument("--micro", type=int, default=1, help="sequences per micro-batch (N>1)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-steps", type=int, default=3, help="tokens in the CPU baseline sample")
-    p.add_argument("--kernel-sweep", action="store_true",
+    p.add_argument("--kernel-sweep", nargs="?", const="all", default=None,
+                   choices=["all", "matvec", "gemm", "attention", "norm"],
                    help="isolated kernel sweep (matvec / tensor-core GEMM shapes, attention lengths, RMSNorm and "
                         "RoPE at hidden 3584): one JSON line per case instead of the decode benchmark")
     p.add_argument("--layers", type=int, default=0,
@@ -360,7 +361,8 @@ def run_kernel_sweep(args):
     import torch
     dllm = importlib.import_module("distributed-llm1_b200")
     torch.cuda.set_device(0)
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream()  # not the legacy default stream: its NULL handle means "the ctx's own stream"
+    torch.cuda.set_stream(stream)  # the L2 flush, the ops and the events all run on it
     peak, peak_kind = measured_peaks()
     flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device="cuda")
     lines = []
@@ -392,10 +394,12 @@ def run_kernel_sweep(args):
     ctx = dllm.initKernels(0, cfg)
     ctx.set_stream(stream.cuda_stream)
     rng = np.random.default_rng(0)
-    for K, N in SWEEP_SHAPES:
+    which = args.kernel_sweep
+    rows = {"all": (1, 16, 64), "matvec": (1,), "gemm": (16, 64)}.get(which, ())
+    for K, N in (SWEEP_SHAPES if rows else []):
         w = ctx.createBf16(K * N, "w")
         ctx.fillNormalBf16(w, K + N, WEIGHT_STD)
-        for n in (1, 16, 64):
+        for n in rows:
             x = ctx.createF32(n * K, "x")
             ctx.writeF32(x, rng.standard_normal(n * K).astype(np.float32))
             # the output buffer is dropped at once and comes back from the ctx's buffer cache
@@ -411,10 +415,13 @@ def run_kernel_sweep(args):
     ctx.writeF32(vc, rng.standard_normal(cfg.max_pos * KD).astype(np.float32))
     q = ctx.createF32(QD, "q")
     ctx.writeF32(q, rng.standard_normal(QD).astype(np.float32))
-    for T in SWEEP_ATTN:
+    for T in (SWEEP_ATTN if which in ("all", "attention") else []):
         sec = timed(lambda: ctx.attention(q, kc, vc, T - 1, 1))
         emit("decode attention (fp32 cache, reference layout)", f"T={T} 28/4 heads hd=128", sec,
              2 * T * KD * 4 + 2 * QD * 4)
+    if which not in ("all", "norm"):
+        ctx.close()
+        return lines
     D = cfg.hidden_size
     h = ctx.createF32(D, "h")
     ctx.writeF32(h, rng.standard_normal(D).astype(np.float32))

@@ -85,7 +85,8 @@ class KernelContext:
             self.handle = None
 
     def set_stream(self, cuda_stream: int | None):
-        """Enqueue on a caller-owned cudaStream_t (e.g. torch.cuda.current_stream().cuda_stream)."""
+        """Enqueue on a caller-owned cudaStream_t (e.g. torch.cuda.Stream().cuda_stream); 0 / None
+        (the legacy default stream's handle) selects the ctx's own stream."""
         self._check(self.lib.dllm_ctx_set_stream(self.handle, cuda_stream or None), "set_stream")
 
     def set_tensor_core_rows(self, min_rows: int):

@@ -235,7 +235,9 @@ def bench_pipeline(args, bench):
                                          max_pos=args.kv_len + steps_total + 16)
     stages = dllm.plan_stages(cfg, world)
     start, end = stages[rank]
-    stream = torch.cuda.current_stream()
+    # a real stream (the legacy default stream's handle is NULL, which the ctx
+    # reads as "use your own stream"): passes and timing events share it
+    stream = torch.cuda.Stream()
     ctx = dllm.initKernels(local, cfg)
     ctx.set_stream(stream.cuda_stream)
     st = dllm.Stage(ctx, start, end)

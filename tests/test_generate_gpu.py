@@ -63,8 +63,11 @@ def test_generate_32_tokens_fp32_kv(dllm, w05, oracle_runs):
 def test_generate_32_tokens_bf16_kv(dllm, w05, oracle_runs):
     """bf16 KV cache: the oracle (bf16-KV mode, and the fp32 reference precision)
     replays the GPU's own token stream; logits within rtol/atol 2e-2 at every
-    step, and every emitted token is the oracle's argmax except where the
-    oracle's top-2 margin is below that tolerance (a near-tie either may take)."""
+    step. Against the bf16-KV oracle (the same KV rounding) every emitted token is
+    the oracle's argmax unless its top-2 margin is below 1e-3 (a tie at the level
+    of fp32 summation order); against the fp32-KV oracle the allowance is the
+    logits tolerance, 2e-2. Per-step margins are printed, so a regression cannot
+    pass as a tie unnoticed."""
     cfg, W = w05
     prompt, _ = oracle_runs
     ctx, ld = build_leader(dllm, cfg, W, "bf16")
@@ -73,16 +76,18 @@ def test_generate_32_tokens_bf16_kv(dllm, w05, oracle_runs):
     ld.onToken = got.append
     ld.generate(prompt, STEPS)
     assert len(got) == STEPS
-    for kv in ("bf16", "f32"):
+    for kv, tie in (("bf16", 1e-3), ("f32", 2e-2)):
         forced = ref.OracleLeader(cfg, ref.Weights(W), kv_dtype=kv).teacher_forced(prompt, got)
-        ties = 0
+        ties, margins = 0, []
         for i, want in enumerate(forced):
             lg = ld.read_logits(i)
             assert_close(lg, want, rtol=2e-2, atol=2e-2, what=f"logits step {i} vs {kv}-KV oracle")
             best = ref.argmax_first(want)
+            margins.append(round(top2_margin(want), 5))
             if got[i] != best:
-                assert top2_margin(want) < 2e-2 and want[got[i]] >= want[best] - 2e-2, f"step {i}: token {got[i]} vs {best}"
+                assert top2_margin(want) < tie and want[got[i]] >= want[best] - tie, f"step {i}: token {got[i]} vs {best}"
                 ties += 1
+        print(f"bf16 KV vs {kv}-KV oracle: {ties} near-tie steps; top-2 margins {margins}")
         assert ties <= 2
     ld.close()
     ctx.close()
