@@ -345,6 +345,74 @@ def run_single(args):
     return res
 
 
+# ---- our arm, one GPU, several sequences per step ---------------------------------------
+def run_single_micro(args):
+    """`--micro m` on one GPU: m sequences decoded together, one pass of m rows per
+    step (Stage.forward_rows with the embedding and LM head fused in): up to 8
+    rows through the persistent stage kernel, 16+ rows through the wide pass whose
+    projections run on the tensor cores (tcgen05). Tokens stay on the device and
+    feed the next step; value = tokens of all sequences per second."""
+    import torch
+    dllm = importlib.import_module("distributed-llm1_b200")
+    m = args.micro
+    cfg = dllm.PRESETS[args.model].with_(kv_dtype="bf16", max_seqs=m,
+                                         max_pos=args.kv_len + args.warmup + args.steps + 16)
+    torch.cuda.set_device(0)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx = dllm.initKernels(0, cfg)
+    ctx.set_stream(stream.cuda_stream)
+    st = dllm.Stage(ctx, 0, cfg.num_layers)
+    bufs = device_weights(ctx, st, cfg, 0, cfg.num_layers, embed=True, head=True)
+    for q in range(m):
+        st.fill_kv_random(q, args.kv_len, seed=1 + q)
+    ctx.synchronize(120000)
+    h = torch.zeros(m, cfg.hidden_size, dtype=torch.float32, device="cuda")
+    tok = (torch.arange(m, dtype=torch.int32, device="cuda") * 7919 + 1000) % cfg.vocab_size
+    seqs = list(range(m))
+
+    def step():
+        st.forward_rows(h.data_ptr(), seqs, tok.data_ptr(), tok.data_ptr())
+
+    for _ in range(args.warmup):
+        step()
+    ctx.synchronize(120000)
+    launches0 = ctx.launch_count
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        ev1.synchronize()
+    ctx.synchronize(120000)
+    ms = ev0.elapsed_time(ev1)
+    tps = args.steps * m / (ms / 1000.0)
+    avg_pos = args.kv_len + args.warmup + (args.steps - 1) / 2.0 + 1
+    one = token_bytes(cfg, cfg.num_layers, head=True, embed=True, kv_positions=avg_pos)
+    kv_one = cfg.num_layers * 2 * cfg.num_kv_heads * cfg.head_dim * 2 * avg_pos
+    step_bytes = one + (m - 1) * (kv_one + 2 * cfg.hidden_size)  # weights once, KV and embedding row per sequence
+    peak, peak_kind = measured_peaks()
+    achieved = step_bytes / (ms / 1000.0 / args.steps) / 1e9
+    wide = m >= 16
+    res = {"metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "bf16", "data": "synthetic: random-init N(0,0.02) bf16 weights (device hash), N(0,1) bf16 KV",
+           "config": {"workload": f"{args.model} greedy decode of {m} sequences per step on one GPU, "
+                                  f"{args.kv_len}-slot synthetic bf16 KV each", "batch": m, "kv_len": args.kv_len,
+                      "parallelism": "pp1", "kv_dtype": "bf16", "weights": "bf16",
+                      "path": "wide pass: tcgen05 projections, one kernel per op" if wide else
+                              "persistent stage kernel, one launch per step"},
+           "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                        "traffic": None, "peak_kind": peak_kind, "algorithmic_bytes_per_launch": step_bytes},
+           "gpu_launches": ctx.launch_count - launches0, "clocks": clk.summary()}
+    del bufs
+    st.close()
+    ctx.close()
+    return res
+
+
 # ---- isolated kernel sweep ------------------------------------------------------------------
 SWEEP_SHAPES = [(896, 1152), (1536, 8960), (3584, 18944), (18944, 3584), (3584, 152064)]
 SWEEP_ATTN = [1024, 4096, 16384, 32768]
@@ -442,6 +510,8 @@ def main():
         return
     if args.impl == "reference":
         res = run_reference(args)
+    elif args.gpus <= 1 and args.micro > 1:
+        res = run_single_micro(args)
     elif args.gpus <= 1:
         res = run_single(args)
     else:

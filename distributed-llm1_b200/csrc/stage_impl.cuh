@@ -9,6 +9,7 @@
 #include "kernels.cuh"
 #include "stage.cuh"
 
+
 namespace dllm {
 
 template <typename KT, int HD, int M>
@@ -99,10 +100,9 @@ __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P)
       gemv_phase<EpiSiluGate, M>(eg, GemvIn{P.h, D, P.m_rows, L.ln2, P.eps}, P.I, sm_g, cta, ncta, ns, 8);
       // ---- down_proj (pipeline.js:73), this CTA's K-slice
       down_partial(L.wd, D, P.I, k0, k1 - k0, slice, P.dpart + (size_t)cta * D);
-      if (!grid_barrier(P.bar_count, P.err)) return;
-      trace();
-      // ---- + residual (pipeline.js:74): per-row sum of the partials
-      residual_reduce(P.dpart, D, ncta, cta, ncta, P.h, smem + P.xs_floats);
+      // the next layer's first q|k|v rows (or the LM head) into L2 while the
+      // partials are reduced (issued before the barrier: measured 0.9 µs per
+      // layer faster than after the reduction)
       if (l + 1 < P.n_layers) {
         const LayerW Ln = P.layers[l + 1];
         const EpiQKV<KT> en{Ln.wq, Ln.wk, Ln.wv, nullptr, nullptr, nullptr, P.NQ, P.KVH, P.HD, P.log2_half};
@@ -111,6 +111,10 @@ __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P)
         const EpiArgmax<M> ep{P.lm_head, P.V, nullptr};
         prefetch_phase(ep, D, P.V, cta, ncta, P.pref_bytes);
       }
+      if (!grid_barrier(P.bar_count, P.err)) return;
+      trace();
+      // ---- + residual (pipeline.js:74): per-row sum of the partials
+      residual_reduce(P.dpart, D, ncta, cta, ncta, P.h, smem + P.xs_floats);
       if (!grid_barrier(P.bar_count, P.err)) return;
       trace();
       continue;
