@@ -529,6 +529,26 @@ int tc_rows(dllm_ctx* c, const float* x, int n, int K, const __nv_bfloat16* w, i
   return DLLM_OK;
 }
 
+// Several projections of the same rows (q|k|v, gate|up) in one tensor-core launch
+// per chunk of kTcMaxRows rows, behind one RMSNorm + hi/lo split.
+int tc_rows_multi(dllm_ctx* c, const float* x, int n, int K, const dllm::TcTarget* t, int nt,
+                  const __nv_bfloat16* norm_w) {
+  int Ns[3];
+  for (int i = 0; i < nt; ++i) Ns[i] = t[i].N;
+  for (int r0 = 0; r0 < n; r0 += dllm::kTcMaxRows) {
+    const int m = std::min(dllm::kTcMaxRows, n - r0);
+    const size_t need = dllm::tc_matmul_multi_scratch_bytes(m, K, Ns, nt, c->sms);
+    if (int rc = ensure_tc_scratch(c, need)) return rc;
+    dllm::TcTarget tt[3];
+    for (int i = 0; i < nt; ++i) tt[i] = dllm::TcTarget{t[i].w, t[i].N, t[i].y + (size_t)r0 * t[i].N, t[i].accumulate};
+    cudaError_t e = dllm::tc_matmul_multi(x + (size_t)r0 * K, m, K, tt, nt, norm_w, c->cfg.rms_norm_eps,
+                                          c->tc_scratch, c->tc_scratch_bytes, c->err_dev, c->sms, c->stream);
+    if (e != cudaSuccess) return set_err(c, DLLM_ECUDA, "tensor-core matmul: %s", cudaGetErrorString(e));
+    c->launches += 2;
+  }
+  return DLLM_OK;
+}
+
 int launch(dllm_stage* s, StageParams& P) {
   dllm_ctx* c = s->ctx;
   int ms = c->sms / (P.m_rows * P.KVH);
@@ -612,17 +632,16 @@ int run_wide(dllm_stage* s, float* h, int n, const RowDesc* rd, const int32_t* t
     }
     for (int l = 0; l < s->nl; ++l) {
       const LayerW& L = s->lw[l];
-      if (int rc = tc_rows(c, hh, m, D, L.wq, QD, s->wq, 0, L.ln1)) return rc;
-      if (int rc = tc_rows(c, hh, m, D, L.wk, KD, s->wk, 0, L.ln1)) return rc;
-      if (int rc = tc_rows(c, hh, m, D, L.wv, KD, s->wv, 0, L.ln1)) return rc;
+      const dllm::TcTarget qkv[3] = {{L.wq, QD, s->wq, 0}, {L.wk, KD, s->wk, 0}, {L.wv, KD, s->wv, 0}};
+      if (int rc = tc_rows_multi(c, hh, m, D, qkv, 3, L.ln1)) return rc;
       CK(c, dllm::op_qkv_post(s->wq, s->wk, s->wv, L.bq, L.bk, L.bv, m, f.num_q_heads, f.num_kv_heads, f.head_dim,
                               c->freq, s->wrows, kv, L.kc, L.vc, f.kv_dtype, c->err_dev, c->stream));
       const dllm::AttnArgs A{s->wq, s->watt, L.kc, L.vc, kv, s->wrows, m, f.num_q_heads, f.num_kv_heads, c->scale,
                              s->wide_splits, s->wpart_o, s->wpart_ml, s->warrive, c->err_dev};
       CK(c, dllm::op_attention_paged(A, f.kv_dtype, f.head_dim, c->sms, c->stream));
       if (int rc = tc_rows(c, s->watt, m, QD, L.wo, D, hh, 1, nullptr)) return rc;
-      if (int rc = tc_rows(c, hh, m, D, L.wg, I, s->wg, 0, L.ln2)) return rc;
-      if (int rc = tc_rows(c, hh, m, D, L.wu, I, s->wu, 0, L.ln2)) return rc;
+      const dllm::TcTarget gu[2] = {{L.wg, I, s->wg, 0}, {L.wu, I, s->wu, 0}};
+      if (int rc = tc_rows_multi(c, hh, m, D, gu, 2, L.ln2)) return rc;
       CK(c, dllm::op_silu_mul(s->wg, s->wu, s->wg, m * I, c->stream));
       if (int rc = tc_rows(c, s->wg, m, I, L.wd, D, hh, 1, nullptr)) return rc;
       c->launches += 3;

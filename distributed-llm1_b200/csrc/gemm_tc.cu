@@ -25,7 +25,8 @@ namespace {
 
 constexpr int kBM = 128;      // weight rows per tile (MMA M)
 constexpr int kBK = 64;       // K per stage: 64 bf16 = 128 bytes, one swizzle row
-constexpr int kStages = 4;
+constexpr int kMaxStages = 8;   // deepest ring (one CTA per SM at 16-32 rows)
+constexpr int kTcMaxTargets = 3;
 constexpr int kTcThreads = 128;
 constexpr int kATileBytes = kBM * kBK * 2;             // 16 KB
 constexpr long long kTcWaitCycles = 1ll << 32;        // ~2 s of SM cycles
@@ -99,37 +100,57 @@ DLLM_DEV void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
 }
 DLLM_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-struct TcArgs {
-  int rows, K, N;
-  int n_kblocks, kb_per_split;
+// One output matrix of a launch: weight tiles [tile_begin, tile_begin + tiles) of
+// the grid belong to it. Several targets that share the activations (q|k|v,
+// gate|up) go in one launch behind one hi/lo split.
+struct TcTargetDev {
   float* out;           // y [rows][N], or partials [splits][rows][N]
+  int N;
+  int tile_begin;
   size_t split_stride;  // elements between splits' partials (0: out is y)
   int accumulate;       // y += (only when out is y)
+};
+
+struct TcArgs {
+  int rows, K;
+  int n_kblocks, kb_per_split;
+  int stages;  // ring depth, <= kMaxStages, sized by the host to the shared memory
+  int n_tgt;
+  TcTargetDev t[kTcMaxTargets];
   int* err;
 };
 
 // RP = padded rows (16, 32, 64, 128); the MMA's N is 2 * RP (x_hi rows, x_lo rows).
 template <int RP>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const TcArgs a) {
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__ CUtensorMap tmW1,
+                   const __grid_constant__ CUtensorMap tmW2, const __grid_constant__ CUtensorMap tmX,
+                   const TcArgs a) {
   constexpr int NMMA = 2 * RP;
   constexpr int kBTileBytes = NMMA * kBK * 2;
   constexpr uint32_t kCols = NMMA < 32 ? 32 : NMMA;  // tensor-memory columns (a power of two >= 32)
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full[kStages], empty[kStages], accum;
+  __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages], accum;
   __shared__ uint32_t tmem_base_s;
   __shared__ volatile int abort_s;
   __shared__ int accum_ok_s;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = a.stages;
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint8_t* sA = base;                       // kStages x 16 KB
-  uint8_t* sB = base + kStages * kATileBytes;  // kStages x kBTileBytes
-  const int tile = blockIdx.x;
+  uint8_t* sA = base;                  // S x 16 KB
+  uint8_t* sB = base + S * kATileBytes;  // S x kBTileBytes
+  // which target this CTA's tile belongs to
+  int m = 0;
+  if (a.n_tgt > 1 && (int)blockIdx.x >= a.t[1].tile_begin) m = 1;
+  if (a.n_tgt > 2 && (int)blockIdx.x >= a.t[2].tile_begin) m = 2;
+  const TcTargetDev tg = a.t[m];
+  const CUtensorMap* tmW = m == 0 ? &tmW0 : (m == 1 ? &tmW1 : &tmW2);
+  const int tile = (int)blockIdx.x - tg.tile_begin;
   const int kb0 = blockIdx.y * a.kb_per_split;
   const int nkb = min(a.n_kblocks, kb0 + a.kb_per_split) - kb0;  // >= 1 (host sizes the splits)
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -151,8 +172,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 0 && lane == 0) {
     // ---- producer: K blocks [kb0, kb0 + nkb) through the ring
     for (int i = 0; i < nkb; ++i) {
-      const int s = i % kStages;
-      const uint32_t ph = (uint32_t)(i / kStages) & 1u;
+      const int s = i % S;
+      const uint32_t ph = (uint32_t)(i / S) & 1u;
       if (!mbar_wait(&empty[s], ph ^ 1u)) {
         atomicExch(a.err, kErrTcWait);
         abort_s = 1;
@@ -161,7 +182,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (abort_s) break;
       mbar_expect_tx(&full[s], (uint32_t)(kATileBytes + kBTileBytes));
       const int kx = (kb0 + i) * kBK;
-      tma_load_2d(sA + s * kATileBytes, &tmW, kx, tile * kBM, &full[s]);
+      tma_load_2d(sA + s * kATileBytes, tmW, kx, tile * kBM, &full[s]);
       tma_load_2d(sB + s * kBTileBytes, &tmX, kx, 0, &full[s]);
       issued = i + 1;
     }
@@ -172,8 +193,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                            | ((uint32_t)(NMMA >> 3) << 17)  // N
                            | ((uint32_t)(kBM >> 4) << 24);  // M = 128; A and B K-major
     for (int i = 0; i < nkb; ++i) {
-      const int s = i % kStages;
-      const uint32_t ph = (uint32_t)(i / kStages) & 1u;
+      const int s = i % S;
+      const uint32_t ph = (uint32_t)(i / S) & 1u;
       if (!mbar_wait(&full[s], ph)) {
         atomicExch(a.err, kErrTcWait);
         abort_s = 1;
@@ -198,7 +219,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   tc_fence_after();
   if (accum_ok_s && !abort_s) {
     const int j = tile * kBM + warp * 32 + lane;  // weight row = TMEM lane
-    float* dst = a.out + (size_t)blockIdx.y * a.split_stride;
+    float* dst = tg.out + (size_t)blockIdx.y * tg.split_stride;
     const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
 #pragma unroll 1
     for (int c0 = 0; c0 < RP; c0 += 8) {
@@ -209,10 +230,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         const int r = c0 + q;
-        if (r < a.rows && j < a.N) {
-          float* d = dst + (size_t)r * a.N + j;
+        if (r < a.rows && j < tg.N) {
+          float* d = dst + (size_t)r * tg.N + j;
           const float v = __uint_as_float(hi[q]) + __uint_as_float(lo[q]);
-          *d = a.accumulate ? __fadd_rn(*d, v) : v;
+          *d = tg.accumulate ? __fadd_rn(*d, v) : v;
         }
       }
     }
@@ -222,7 +243,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // ---- teardown: copies still in flight (only after an aborted wait) land
   // before the CTA exits, then the tensor memory is freed
   if (warp == 0 && lane == 0 && abort_s) {
-    for (int i = max(0, issued - kStages); i < issued; ++i) mbar_wait(&full[i % kStages], (uint32_t)(i / kStages) & 1u);
+    for (int i = max(0, issued - S); i < issued; ++i) mbar_wait(&full[i % S], (uint32_t)(i / S) & 1u);
   }
   tc_fence_before();
   __syncthreads();
@@ -313,13 +334,23 @@ int padded_rows(int rows) { return rows <= 16 ? 16 : rows <= 32 ? 32 : rows <= 6
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 struct Plan {
-  int rp, n_tiles, n_kb, kb_per, splits;
-  size_t xb_bytes, part_bytes;
+  int rp, n_tiles, n_kb, kb_per, splits, stages;
+  size_t xb_bytes, part_bytes, smem;
 };
-Plan make_plan(int rows, int K, int N, int sms) {
+
+// Tiles of all targets, K split until tiles x splits fills the SMs, and the ring
+// depth: one wave -> one CTA per SM with the deepest ring that fits (up to 8
+// stages, ~220 KB); several waves -> two CTAs per SM (~110 KB each), so one
+// CTA's epilogue overlaps the other's loads.
+Plan make_plan(int rows, int K, const int* Ns, int n, int sms) {
   Plan p;
   p.rp = padded_rows(rows);
-  p.n_tiles = (N + kBM - 1) / kBM;
+  p.n_tiles = 0;
+  int sumN = 0;
+  for (int i = 0; i < n; ++i) {
+    p.n_tiles += (Ns[i] + kBM - 1) / kBM;
+    sumN += Ns[i];
+  }
   p.n_kb = (K + kBK - 1) / kBK;
   int splits = sms / p.n_tiles;
   if (splits < 1) splits = 1;
@@ -327,24 +358,29 @@ Plan make_plan(int rows, int K, int N, int sms) {
   p.kb_per = (p.n_kb + splits - 1) / splits;
   p.splits = (p.n_kb + p.kb_per - 1) / p.kb_per;  // no empty split
   p.xb_bytes = align_up((size_t)2 * p.rp * K * 2, 1024);
-  p.part_bytes = p.splits > 1 ? (size_t)p.splits * rows * N * 4 : 0;
+  p.part_bytes = p.splits > 1 ? (size_t)p.splits * rows * sumN * 4 : 0;
+  const size_t per_stage = (size_t)kATileBytes + 2 * p.rp * kBK * 2;
+  const bool one_wave = (long long)p.n_tiles * p.splits <= sms;
+  const size_t budget = one_wave ? 220 * 1024 : 110 * 1024;
+  int st = (int)((budget - 1024) / per_stage);
+  p.stages = st < 2 ? 2 : (st > kMaxStages ? kMaxStages : st);
+  p.smem = 1024 + (size_t)p.stages * per_stage;
   return p;
 }
 
 template <int RP>
-size_t smem_bytes() {
-  return 1024 + (size_t)kStages * (kATileBytes + 2 * RP * kBK * 2);
-}
-
-template <int RP>
-cudaError_t launch_rp(const CUtensorMap& tw, const CUtensorMap& tx, const TcArgs& a, dim3 grid, cudaStream_t st) {
+cudaError_t launch_rp(const CUtensorMap* tw, const CUtensorMap& tx, const TcArgs& a, dim3 grid, size_t smem,
+                      cudaStream_t st) {
   static std::once_flag once;
   static cudaError_t attr = cudaSuccess;
   std::call_once(once, [] {
-    attr = cudaFuncSetAttribute(tc_gemm_kernel<RP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes<RP>());
+    const size_t most = 1024 + (size_t)kMaxStages * (kATileBytes + 2 * RP * kBK * 2);
+    const size_t cap = 1024 + 220 * 1024;
+    attr = cudaFuncSetAttribute(tc_gemm_kernel<RP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)(most < cap ? most : cap));
   });
   if (attr != cudaSuccess) return attr;
-  tc_gemm_kernel<RP><<<grid, kTcThreads, smem_bytes<RP>(), st>>>(tw, tx, a);
+  tc_gemm_kernel<RP><<<grid, kTcThreads, smem, st>>>(tw[0], tw[1], tw[2], tx, a);
   return cudaGetLastError();
 }
 
@@ -352,49 +388,85 @@ cudaError_t launch_rp(const CUtensorMap& tw, const CUtensorMap& tx, const TcArgs
 
 bool tc_available() { return encode_fn() != nullptr; }
 
-size_t tc_matmul_scratch_bytes(int rows, int K, int N, int sms) {
-  const Plan p = make_plan(rows, K, N, sms);
+size_t tc_matmul_scratch_bytes(int rows, int K, int N, int sms) { return tc_matmul_multi_scratch_bytes(rows, K, &N, 1, sms); }
+
+size_t tc_matmul_multi_scratch_bytes(int rows, int K, const int* Ns, int n, int sms) {
+  const Plan p = make_plan(rows, K, Ns, n, sms);
   return p.xb_bytes + p.part_bytes;
 }
 
-cudaError_t tc_matmul(const float* x, int rows, int K, const __nv_bfloat16* w, int N, float* y, int accumulate,
-                      const __nv_bfloat16* norm_w, float eps, void* scratch, size_t scratch_bytes, int* err, int sms,
-                      cudaStream_t st) {
-  if (rows < 1 || rows > kTcMaxRows || K < 8 || K % 8 != 0 || N < 1 || !x || !w || !y || !scratch || !err)
+cudaError_t tc_matmul_multi(const float* x, int rows, int K, const TcTarget* t, int n, const __nv_bfloat16* norm_w,
+                            float eps, void* scratch, size_t scratch_bytes, int* err, int sms, cudaStream_t st) {
+  if (rows < 1 || rows > kTcMaxRows || K < 8 || K % 8 != 0 || n < 1 || n > kTcMaxTargets || !x || !t || !scratch ||
+      !err)
     return cudaErrorInvalidValue;
-  if ((reinterpret_cast<uintptr_t>(w) & 15) != 0 || (reinterpret_cast<uintptr_t>(scratch) & 255) != 0)
-    return cudaErrorMisalignedAddress;
-  const Plan p = make_plan(rows, K, N, sms);
+  if ((reinterpret_cast<uintptr_t>(scratch) & 255) != 0) return cudaErrorMisalignedAddress;
+  int Ns[kTcMaxTargets];
+  for (int i = 0; i < n; ++i) {
+    if (!t[i].w || !t[i].y || t[i].N < 1) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(t[i].w) & 15) != 0) return cudaErrorMisalignedAddress;
+    Ns[i] = t[i].N;
+  }
+  const Plan p = make_plan(rows, K, Ns, n, sms);
   if (p.xb_bytes + p.part_bytes > scratch_bytes) return cudaErrorInvalidValue;
   __nv_bfloat16* xb = static_cast<__nv_bfloat16*>(scratch);
   float* part = reinterpret_cast<float*>(static_cast<char*>(scratch) + p.xb_bytes);
   split_hilo_kernel<<<p.rp, 256, 0, st>>>(x, rows, K, norm_w, eps, p.rp, xb);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  CUtensorMap tw, tx;
-  if (!encode_rows(&tw, w, K, N, kBM) || !encode_rows(&tx, xb, K, 2 * p.rp, 2 * p.rp)) return cudaErrorInvalidValue;
-  TcArgs a;
+  CUtensorMap tw[kTcMaxTargets], tx;
+  TcArgs a = {};
   a.rows = rows;
   a.K = K;
-  a.N = N;
   a.n_kblocks = p.n_kb;
   a.kb_per_split = p.kb_per;
-  a.out = p.splits > 1 ? part : y;
-  a.split_stride = p.splits > 1 ? (size_t)rows * N : 0;
-  a.accumulate = p.splits > 1 ? 0 : accumulate;
+  a.stages = p.stages;
+  a.n_tgt = n;
   a.err = err;
+  int tile = 0;
+  size_t part_off = 0;
+  for (int i = 0; i < n; ++i) {
+    if (!encode_rows(&tw[i], t[i].w, K, t[i].N, kBM)) return cudaErrorInvalidValue;
+    a.t[i].N = t[i].N;
+    a.t[i].tile_begin = tile;
+    tile += (t[i].N + kBM - 1) / kBM;
+    if (p.splits > 1) {
+      a.t[i].out = part + part_off;
+      a.t[i].split_stride = (size_t)rows * t[i].N;
+      a.t[i].accumulate = 0;
+      part_off += (size_t)p.splits * rows * t[i].N;
+    } else {
+      a.t[i].out = t[i].y;
+      a.t[i].split_stride = 0;
+      a.t[i].accumulate = t[i].accumulate;
+    }
+  }
+  for (int i = n; i < kTcMaxTargets; ++i) tw[i] = tw[0];  // unused parameters
+  if (!encode_rows(&tx, xb, K, 2 * p.rp, 2 * p.rp)) return cudaErrorInvalidValue;
   const dim3 grid(p.n_tiles, p.splits);
   switch (p.rp) {
-    case 16: e = launch_rp<16>(tw, tx, a, grid, st); break;
-    case 32: e = launch_rp<32>(tw, tx, a, grid, st); break;
-    case 64: e = launch_rp<64>(tw, tx, a, grid, st); break;
-    default: e = launch_rp<128>(tw, tx, a, grid, st); break;
+    case 16: e = launch_rp<16>(tw, tx, a, grid, p.smem, st); break;
+    case 32: e = launch_rp<32>(tw, tx, a, grid, p.smem, st); break;
+    case 64: e = launch_rp<64>(tw, tx, a, grid, p.smem, st); break;
+    default: e = launch_rp<128>(tw, tx, a, grid, p.smem, st); break;
   }
   if (e != cudaSuccess || p.splits == 1) return e;
-  const size_t total = (size_t)rows * N;
-  unsigned int blocks = (unsigned int)std::min<size_t>((total + 255) / 256, (size_t)sms * 8);
-  splitk_reduce_kernel<<<blocks, 256, 0, st>>>(part, p.splits, (size_t)rows * N, rows, N, y, accumulate);
-  return cudaGetLastError();
+  for (int i = 0; i < n; ++i) {
+    const size_t total = (size_t)rows * t[i].N;
+    const unsigned int blocks = (unsigned int)std::min<size_t>((total + 255) / 256, (size_t)sms * 8);
+    splitk_reduce_kernel<<<blocks, 256, 0, st>>>(a.t[i].out, p.splits, a.t[i].split_stride, rows, t[i].N, t[i].y,
+                                                 t[i].accumulate);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t tc_matmul(const float* x, int rows, int K, const __nv_bfloat16* w, int N, float* y, int accumulate,
+                      const __nv_bfloat16* norm_w, float eps, void* scratch, size_t scratch_bytes, int* err, int sms,
+                      cudaStream_t st) {
+  const TcTarget t{w, N, y, accumulate};
+  return tc_matmul_multi(x, rows, K, &t, 1, norm_w, eps, scratch, scratch_bytes, err, sms, st);
 }
 
 }  // namespace dllm

@@ -35,6 +35,19 @@ cudaError_t tc_matmul(const float* x, int rows, int K, const __nv_bfloat16* w, i
                       const __nv_bfloat16* norm_w, float eps, void* scratch, size_t scratch_bytes, int* err, int sms,
                       cudaStream_t st);
 
+// One output of a launch that shares its activations with the others (the
+// q|k|v or gate|up projections of one RMSNorm'd input).
+struct TcTarget {
+  const __nv_bfloat16* w;  // [N, K] bf16, 16-byte aligned
+  int N;
+  float* y;                // [rows, N]
+  int accumulate;          // 0 store, 1 add to y
+};
+// Up to 3 targets in one launch behind one hi/lo split of x (and one RMSNorm).
+size_t tc_matmul_multi_scratch_bytes(int rows, int K, const int* Ns, int n, int sms);
+cudaError_t tc_matmul_multi(const float* x, int rows, int K, const TcTarget* t, int n, const __nv_bfloat16* norm_w,
+                            float eps, void* scratch, size_t scratch_bytes, int* err, int sms, cudaStream_t st);
+
 // Whether the driver offers the tensor-map encoder (always true on a B200 driver).
 bool tc_available();
 
