@@ -50,7 +50,10 @@ def parse_args():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--model", default="qwen2.5-7b")
     p.add_argument("--kv-len", type=int, default=KV_LEN)
-    p.add_argument("--micro", type=int, default=1, help="sequences per micro-batch (N>1)")
+    p.add_argument("--micro", type=int, default=1,
+                   help="sequences per micro-batch (N>1), or sequences decoded together (N=1)")
+    p.add_argument("--tc-rows", type=int, default=None,
+                   help="passes of at least this many rows use the tensor-core pass (0: never; default: the library's)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-steps", type=int, default=3, help="tokens in the CPU baseline sample")
     p.add_argument("--kernel-sweep", nargs="?", const="all", default=None,
@@ -362,6 +365,8 @@ def run_single_micro(args):
     torch.cuda.set_stream(stream)
     ctx = dllm.initKernels(0, cfg)
     ctx.set_stream(stream.cuda_stream)
+    if args.tc_rows is not None:
+        ctx.set_tensor_core_rows(args.tc_rows)
     st = dllm.Stage(ctx, 0, cfg.num_layers)
     bufs = device_weights(ctx, st, cfg, 0, cfg.num_layers, embed=True, head=True)
     for q in range(m):
@@ -395,7 +400,8 @@ def run_single_micro(args):
     step_bytes = one + (m - 1) * (kv_one + 2 * cfg.hidden_size)  # weights once, KV and embedding row per sequence
     peak, peak_kind = measured_peaks()
     achieved = step_bytes / (ms / 1000.0 / args.steps) / 1e9
-    wide = m >= 16
+    tc = 8 if args.tc_rows is None else args.tc_rows
+    wide = tc > 0 and m >= tc
     res = {"metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
            "dtype": "bf16", "data": "synthetic: random-init N(0,0.02) bf16 weights (device hash), N(0,1) bf16 KV",
@@ -403,7 +409,8 @@ def run_single_micro(args):
                                   f"{args.kv_len}-slot synthetic bf16 KV each", "batch": m, "kv_len": args.kv_len,
                       "parallelism": "pp1", "kv_dtype": "bf16", "weights": "bf16",
                       "path": "wide pass: tcgen05 projections, one kernel per op" if wide else
-                              "persistent stage kernel, one launch per step"},
+                              "persistent stage kernel, one launch per step",
+                      "tensor_core_rows": args.tc_rows},
            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                         "traffic": None, "peak_kind": peak_kind, "algorithmic_bytes_per_launch": step_bytes},
            "gpu_launches": ctx.launch_count - launches0, "clocks": clk.summary()}

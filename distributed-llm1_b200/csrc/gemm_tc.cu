@@ -3,7 +3,8 @@
 // One CTA = 4 warps computes a 128-row weight tile against all (padded) rows
 // of the pass over a contiguous range of K (split-K when the tiles alone do not
 // fill the GPU). Warp 0 lane 0 streams the weight tile and the activation tile
-// of each 64-wide K block into a 4-stage shared-memory ring with TMA
+// of each 128-wide K block (two 64-wide boxes) into a shared-memory ring of 2-8
+// stages with TMA
 // (cp.async.bulk.tensor, 128-byte swizzle, completion on an mbarrier); warp 1
 // lane 0 issues tcgen05.mma (kind::f16, bf16 in, fp32 accumulator in tensor
 // memory) and frees each stage with tcgen05.commit; then all four warps read the
@@ -24,11 +25,14 @@ namespace dllm {
 namespace {
 
 constexpr int kBM = 128;      // weight rows per tile (MMA M)
-constexpr int kBK = 64;       // K per stage: 64 bf16 = 128 bytes, one swizzle row
+constexpr int kBK = 64;       // K per box: 64 bf16 = 128 bytes, one swizzle row
+constexpr int kBoxes = 2;     // boxes per stage: 256 contiguous bytes of each weight row per stage
+constexpr int kBKS = kBK * kBoxes;  // K per stage
 constexpr int kMaxStages = 8;   // deepest ring (one CTA per SM at 16-32 rows)
 constexpr int kTcMaxTargets = 3;
 constexpr int kTcThreads = 128;
-constexpr int kATileBytes = kBM * kBK * 2;             // 16 KB
+constexpr int kABoxBytes = kBM * kBK * 2;              // 16 KB: one 128-row box
+constexpr int kATileBytes = kABoxBytes * kBoxes;        // 32 KB per stage
 constexpr long long kTcWaitCycles = 1ll << 32;        // ~2 s of SM cycles
 
 DLLM_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -127,7 +131,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                    const __grid_constant__ CUtensorMap tmW2, const __grid_constant__ CUtensorMap tmX,
                    const TcArgs a) {
   constexpr int NMMA = 2 * RP;
-  constexpr int kBTileBytes = NMMA * kBK * 2;
+  constexpr int kBBoxBytes = NMMA * kBK * 2;
+  constexpr int kBTileBytes = kBBoxBytes * kBoxes;
   constexpr uint32_t kCols = NMMA < 32 ? 32 : NMMA;  // tensor-memory columns (a power of two >= 32)
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages], accum;
@@ -148,6 +153,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int tile = (int)blockIdx.x - tg.tile_begin;
   const int kb0 = blockIdx.y * a.kb_per_split;
   const int nkb = min(a.n_kblocks, kb0 + a.kb_per_split) - kb0;  // >= 1 (host sizes the splits)
+  const int rot = (int)((blockIdx.x * 5u + blockIdx.y * 3u) % (unsigned)nkb);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -181,9 +187,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       if (abort_s) break;
       mbar_expect_tx(&full[s], (uint32_t)(kATileBytes + kBTileBytes));
-      const int kx = (kb0 + i) * kBK;
-      tma_load_2d(sA + s * kATileBytes, tmW, kx, tile * kBM, &full[s]);
-      tma_load_2d(sB + s * kBTileBytes, &tmX, kx, 0, &full[s]);
+      // K blocks in a per-tile rotated order: 148 tiles reading the same column
+      // offset of rows a fixed stride apart crowd a few DRAM channels
+      const int kx = (kb0 + (i + rot) % nkb) * kBKS;
+#pragma unroll
+      for (int b = 0; b < kBoxes; ++b) {
+        tma_load_2d(sA + s * kATileBytes + b * kABoxBytes, tmW, kx + b * kBK, tile * kBM, &full[s]);
+        tma_load_2d(sB + s * kBTileBytes + b * kBBoxBytes, &tmX, kx + b * kBK, 0, &full[s]);
+      }
       issued = i + 1;
     }
   } else if (warp == 1 && lane == 0) {
@@ -202,11 +213,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       if (abort_s) break;
       tc_fence_after();
-      const uint64_t ad = umma_desc_sw128(sA + s * kATileBytes);
-      const uint64_t bd = umma_desc_sw128(sB + s * kBTileBytes);
 #pragma unroll
-      for (int kk = 0; kk < kBK / 16; ++kk)  // +32 bytes along K inside the swizzled row
-        umma_bf16(tmem, ad + 2ull * kk, bd + 2ull * kk, idesc, (uint32_t)((i | kk) != 0));
+      for (int b = 0; b < kBoxes; ++b) {
+        const uint64_t ad = umma_desc_sw128(sA + s * kATileBytes + b * kABoxBytes);
+        const uint64_t bd = umma_desc_sw128(sB + s * kBTileBytes + b * kBBoxBytes);
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk)  // +32 bytes along K inside the swizzled row
+          umma_bf16(tmem, ad + 2ull * kk, bd + 2ull * kk, idesc, (uint32_t)((i | b | kk) != 0));
+      }
       umma_commit(&empty[s]);
     }
     umma_commit(&accum);  // every MMA issued above has completed when this arrives
@@ -255,40 +269,72 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
 // x (fp32 [rows][K]) -> xb (bf16 [2 RP][K]): row t < rows: xb[t] = bf16(x'), xb[RP + t]
 // = bf16(x' - bf16(x')), where x' = (x * rsqrt(mean(x^2) + eps)) * g with a norm,
-// else x; rows [rows, RP) are zero. One block per padded row.
-__global__ void split_hilo_kernel(const float* x, int rows, int K, const __nv_bfloat16* norm_w, float eps, int rp,
-                                  __nv_bfloat16* xb) {
-  __shared__ float red[32];
-  const int t = blockIdx.x;
-  __nv_bfloat16* hi = xb + (size_t)t * K;
-  __nv_bfloat16* lo = xb + (size_t)(rp + t) * K;
+// else x; rows [rows, RP) are zero. Grid (K / kSplitChunk chunks, RP rows), 256
+// threads x 8 elements each, 16-byte loads and stores: no thread walks a row
+// (a strided loop over K is a chain of dependent round trips). With a norm each
+// block first sums the squares of its whole row (float4 loads, block reduce), so
+// every chunk of a row uses the same scale.
+constexpr int kSplitThreads = 256;
+constexpr int kSplitChunk = kSplitThreads * 8;
+
+__global__ void __launch_bounds__(kSplitThreads) split_hilo_kernel(const float* x, int rows, int K,
+                                                                   const __nv_bfloat16* norm_w, float eps, int rp,
+                                                                   __nv_bfloat16* xb) {
+  __shared__ float red[kSplitThreads / 32];
+  const int t = blockIdx.y;
+  const int k = blockIdx.x * kSplitChunk + threadIdx.x * 8;
+  uint4* hi = reinterpret_cast<uint4*>(xb + (size_t)t * K + k);
+  uint4* lo = reinterpret_cast<uint4*>(xb + (size_t)(rp + t) * K + k);
   if (t >= rows) {
-    for (int k = threadIdx.x; k < K; k += blockDim.x) {
-      hi[k] = __float2bfloat16_rn(0.f);
-      lo[k] = __float2bfloat16_rn(0.f);
+    if (k < K) {
+      *hi = make_uint4(0u, 0u, 0u, 0u);
+      *lo = make_uint4(0u, 0u, 0u, 0u);
     }
     return;
   }
   const float* xr = x + (size_t)t * K;
   float scale = 1.f;
   if (norm_w) {
+    const float4* x4 = reinterpret_cast<const float4*>(xr);
     float ss = 0.f;
-    for (int k = threadIdx.x; k < K; k += blockDim.x) ss = fmaf(xr[k], xr[k], ss);
+    for (int i = threadIdx.x; i < (K >> 2); i += kSplitThreads) {
+      const float4 v = __ldg(x4 + i);
+      ss = fmaf(v.x, v.x, ss);
+      ss = fmaf(v.y, v.y, ss);
+      ss = fmaf(v.z, v.z, ss);
+      ss = fmaf(v.w, v.w, ss);
+    }
     ss = warp_sum(ss);
-    const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    if ((threadIdx.x & 31) == 0) red[w] = ss;
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
     __syncthreads();
     float tot = 0.f;
-    for (int i = 0; i < nw; ++i) tot += red[i];
+    for (int i = 0; i < kSplitThreads / 32; ++i) tot += red[i];
     scale = 1.0f / sqrtf(tot / (float)K + eps);
   }
-  for (int k = threadIdx.x; k < K; k += blockDim.x) {
-    float v = xr[k];
-    if (norm_w) v = (v * scale) * bf16_to_f32(norm_w[k]);
-    const __nv_bfloat16 h = __float2bfloat16_rn(v);
-    hi[k] = h;
-    lo[k] = __float2bfloat16_rn(v - bf16_to_f32(h));
+  if (k >= K) return;
+  const float4 a = __ldg(reinterpret_cast<const float4*>(xr + k));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(xr + k + 4));
+  float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  if (norm_w) {
+    const uint4 g = __ldg(reinterpret_cast<const uint4*>(norm_w + k));
+    const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      v[2 * q] = (v[2 * q] * scale) * bf16_lo(gw[q]);
+      v[2 * q + 1] = (v[2 * q + 1] * scale) * bf16_hi(gw[q]);
+    }
   }
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const __nv_bfloat16 h0 = __float2bfloat16_rn(v[2 * q]), h1 = __float2bfloat16_rn(v[2 * q + 1]);
+    const __nv_bfloat16 l0 = __float2bfloat16_rn(v[2 * q] - bf16_to_f32(h0));
+    const __nv_bfloat16 l1 = __float2bfloat16_rn(v[2 * q + 1] - bf16_to_f32(h1));
+    h[q] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+    l[q] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
+  }
+  *hi = make_uint4(h[0], h[1], h[2], h[3]);
+  *lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
 // y[t][j] (=|+=) sum over splits s of part[s][t][j], in split order.
@@ -351,7 +397,7 @@ Plan make_plan(int rows, int K, const int* Ns, int n, int sms) {
     p.n_tiles += (Ns[i] + kBM - 1) / kBM;
     sumN += Ns[i];
   }
-  p.n_kb = (K + kBK - 1) / kBK;
+  p.n_kb = (K + kBKS - 1) / kBKS;
   int splits = sms / p.n_tiles;
   if (splits < 1) splits = 1;
   if (splits > p.n_kb) splits = p.n_kb;
@@ -359,9 +405,11 @@ Plan make_plan(int rows, int K, const int* Ns, int n, int sms) {
   p.splits = (p.n_kb + p.kb_per - 1) / p.kb_per;  // no empty split
   p.xb_bytes = align_up((size_t)2 * p.rp * K * 2, 1024);
   p.part_bytes = p.splits > 1 ? (size_t)p.splits * rows * sumN * 4 : 0;
-  const size_t per_stage = (size_t)kATileBytes + 2 * p.rp * kBK * 2;
+  const size_t per_stage = (size_t)kATileBytes + (size_t)kBoxes * 2 * p.rp * kBK * 2;
   const bool one_wave = (long long)p.n_tiles * p.splits <= sms;
-  const size_t budget = one_wave ? 220 * 1024 : 110 * 1024;
+  // two CTAs per SM only when each still gets a double-buffered ring
+  const bool two_per_sm = !one_wave && (110 * 1024 - 1024) / per_stage >= 2;
+  const size_t budget = two_per_sm ? 110 * 1024 : 220 * 1024;
   int st = (int)((budget - 1024) / per_stage);
   p.stages = st < 2 ? 2 : (st > kMaxStages ? kMaxStages : st);
   p.smem = 1024 + (size_t)p.stages * per_stage;
@@ -374,7 +422,7 @@ cudaError_t launch_rp(const CUtensorMap* tw, const CUtensorMap& tx, const TcArgs
   static std::once_flag once;
   static cudaError_t attr = cudaSuccess;
   std::call_once(once, [] {
-    const size_t most = 1024 + (size_t)kMaxStages * (kATileBytes + 2 * RP * kBK * 2);
+    const size_t most = 1024 + (size_t)kMaxStages * (kATileBytes + kBoxes * 2 * RP * kBK * 2);
     const size_t cap = 1024 + 220 * 1024;
     attr = cudaFuncSetAttribute(tc_gemm_kernel<RP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)(most < cap ? most : cap));
@@ -411,7 +459,10 @@ cudaError_t tc_matmul_multi(const float* x, int rows, int K, const TcTarget* t, 
   if (p.xb_bytes + p.part_bytes > scratch_bytes) return cudaErrorInvalidValue;
   __nv_bfloat16* xb = static_cast<__nv_bfloat16*>(scratch);
   float* part = reinterpret_cast<float*>(static_cast<char*>(scratch) + p.xb_bytes);
-  split_hilo_kernel<<<p.rp, 256, 0, st>>>(x, rows, K, norm_w, eps, p.rp, xb);
+  if ((reinterpret_cast<uintptr_t>(x) & 15) != 0 || (norm_w && (reinterpret_cast<uintptr_t>(norm_w) & 15) != 0))
+    return cudaErrorMisalignedAddress;
+  split_hilo_kernel<<<dim3((K + kSplitChunk - 1) / kSplitChunk, p.rp), kSplitThreads, 0, st>>>(x, rows, K, norm_w,
+                                                                                               eps, p.rp, xb);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   CUtensorMap tw[kTcMaxTargets], tx;

@@ -18,7 +18,7 @@
 
 namespace dllm {
 
-constexpr int kTcMinRows = 16;   // passes with fewer rows stay on the CUDA-core matvec
+constexpr int kTcMinRows = 8;    // passes with fewer rows stay on the CUDA-core matvec (measured crossover)
 constexpr int kTcMaxRows = 128;  // rows per launch (x_hi + x_lo = 256 MMA columns)
 constexpr int kErrTcWait = 5;    // a tcgen05 kernel gave up waiting on an mbarrier
 

@@ -90,7 +90,7 @@ class KernelContext:
         self._check(self.lib.dllm_ctx_set_stream(self.handle, cuda_stream or None), "set_stream")
 
     def set_tensor_core_rows(self, min_rows: int):
-        """Passes of >= min_rows rows use the tcgen05 GEMM (0: never); default 16."""
+        """Passes of >= min_rows rows use the tcgen05 GEMM (0: never); default 8."""
         self._check(self.lib.dllm_ctx_set_tensor_core_rows(self.handle, int(min_rows)), "set_tensor_core_rows")
 
     def synchronize(self, timeout_ms: int = 15000):

@@ -93,7 +93,8 @@ uint64_t dllm_ctx_launch_count(const dllm_ctx* ctx);
 /* Passes of at least `min_rows` rows (MATMUL with n > 1, kernels.js:26-44; prefill
  * chunks and wide micro-batches of Stage.forward, pipeline.js:48-78) run their
  * projections as tcgen05 tensor-core GEMMs; fewer rows use the CUDA-core matvec.
- * Default 16; 0 keeps every pass on the matvec; otherwise 2..128. */
+ * Default 8 (at 7B, 8 rows take 14.4 ms through the persistent kernel and ~7 ms
+ * through the tensor-core pass); 0 keeps every pass on the matvec; otherwise 2..128. */
 int dllm_ctx_set_tensor_core_rows(dllm_ctx* ctx, int min_rows);
 
 /* ---- buffers (kernels.js:181-211) ----------------------------------------- */

@@ -92,7 +92,7 @@ def test_tc_and_cuda_core_paths_agree(ctx7):
     try:
         cc = ctx7.readF32(ctx7.matmul(xb, w, n, K, N), n * N)
     finally:
-        ctx7.set_tensor_core_rows(16)
+        ctx7.set_tensor_core_rows(8)
     scale = float(np.max(np.abs(cc)))
     assert_close(tc, cc, rtol=1e-3, atol=1e-4 * scale, what="tensor-core vs CUDA-core matmul")
 

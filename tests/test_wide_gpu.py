@@ -94,7 +94,7 @@ def test_wide_microbatch_16_sequences_matches_oracle(dllm):
         ctx.synchronize()
         outs[mode] = (h.cpu().numpy(), tout.cpu().numpy())
         assert [st.t0_of(s) for s in range(B)] == [n + 1 for n in lens]
-    ctx.set_tensor_core_rows(16)
+    ctx.set_tensor_core_rows(8)
     lib = _lib()
     ocfg = _oracle_cfg(cfg)
     for s in range(B):
