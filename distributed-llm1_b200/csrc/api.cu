@@ -101,9 +101,9 @@ struct dllm_stage {
   float *h = nullptr, *q = nullptr, *att = nullptr, *mid = nullptr;
   float *part_o = nullptr, *part_ml = nullptr;
   unsigned int* arrive = nullptr;
-  float* dpart = nullptr;  // split-K MLP partials [sms][D]
+  float* h2 = nullptr;     // split-K MLP: the folded hidden row [D] o_proj adds to
   RowDesc* rows = nullptr;
-  unsigned int* bar = nullptr;  // [count, epoch]
+  unsigned int* bar = nullptr;  // [count, epoch, -, -] then the split-K MLP's fixed-point sums [D] (i64)
   unsigned long long* best = nullptr;
   int32_t* tok = nullptr;       // [8]
   // API forwards with many rows
@@ -481,7 +481,8 @@ StageParams base_params(dllm_stage* s) {
   P.part_o = s->part_o;
   P.part_ml = s->part_ml;
   P.arrive = s->arrive;
-  P.dpart = s->dpart;
+  P.h2 = s->h2;
+  P.acc = reinterpret_cast<long long*>(s->bar + 4);
   P.kv = stage_kv(s);
   P.embed = s->embed;
   P.final_norm = s->norm;
@@ -1221,9 +1222,9 @@ int dllm_stage_create(dllm_ctx* c, int start, int end, dllm_stage** out) {
   if (!rc) rc = dev_alloc(c, &s->part_o, R * f.num_q_heads * kMaxSplitsAlloc * f.head_dim, "attn partials");
   if (!rc) rc = dev_alloc(c, &s->part_ml, R * f.num_q_heads * kMaxSplitsAlloc * 2, "attn partials");
   if (!rc) rc = dev_alloc(c, &s->arrive, 2 * R * f.num_kv_heads, "attn tickets");  // arrivals, finishes
-  if (!rc) rc = dev_alloc(c, &s->dpart, (size_t)c->sms * D, "mlp partials");
+  if (!rc) rc = dev_alloc(c, &s->h2, D, "folded hidden row");
   if (!rc) rc = dev_alloc(c, &s->rows, R, "rows");
-  if (!rc) rc = dev_alloc(c, &s->bar, 2, "barrier");
+  if (!rc) rc = dev_alloc(c, &s->bar, 4 + 2 * D, "barrier + mlp sums");
   if (!rc) rc = dev_alloc(c, &s->best, R, "argmax keys");
   if (!rc) rc = dev_alloc(c, &s->tok, R, "tokens");
   if (!rc) {
@@ -1255,7 +1256,7 @@ void dllm_stage_destroy(dllm_stage* s) {
   dev_free(s->part_o);
   dev_free(s->part_ml);
   dev_free(s->arrive);
-  dev_free(s->dpart);
+  dev_free(s->h2);
   dev_free(s->rows);
   dev_free(s->bar);
   dev_free(s->best);

@@ -144,7 +144,35 @@ struct GemvIn {
   int m_rows;                   // valid rows (<= M)
   const __nv_bfloat16* norm_w;  // RMSNorm gamma [K] or null
   float eps;
+  const long long* acc = nullptr;  // one row: pending fixed-point down_proj sums [K] added to x
+  float* save = nullptr;           // optional [m_rows][K]: this CTA's share of the (summed) input rows
 };
+
+// ---- fixed-point residual sums (one-row split-K MLP) --------------------------------
+// Each CTA's down_proj partial is rounded to a multiple of 2^-32 and added into a
+// 64-bit integer accumulator with an atomic: integer addition is associative, so
+// the sum is the same whatever order the 148 CTAs arrive in (deterministic), and
+// it is exact up to the one rounding per partial (<= 2^-33 each). Range: partials
+// below 2^31 in magnitude.
+constexpr float kFixScale = 4294967296.0f;            // 2^32
+constexpr float kFixInv = 2.3283064365386963e-10f;    // 2^-32
+DLLM_DEV long long f32_to_fix(float v) { return __float2ll_rn(v * kFixScale); }
+DLLM_DEV float fix_to_f32(long long a) { return __ll2float_rn(a) * kFixInv; }
+
+// Elements [e, e+4) of row m of the phase input: x plus, when the input carries
+// them, the pending fixed-point sums (e a multiple of 4).
+DLLM_DEV float4 load_in4(const GemvIn& in, int m, int e) {
+  float4 v = __ldcg(reinterpret_cast<const float4*>(in.x + (size_t)m * in.K + e));
+  if (in.acc) {
+    const longlong2* a = reinterpret_cast<const longlong2*>(in.acc + e);
+    const longlong2 a0 = __ldcg(a), a1 = __ldcg(a + 1);
+    v.x = __fadd_rn(v.x, fix_to_f32(a0.x));
+    v.y = __fadd_rn(v.y, fix_to_f32(a0.y));
+    v.z = __fadd_rn(v.z, fix_to_f32(a1.x));
+    v.w = __fadd_rn(v.w, fix_to_f32(a1.y));
+  }
+  return v;
+}
 
 template <int M>
 DLLM_DEV void row_scales(const GemvIn& in, float* red, float (&scale)[M]) {
@@ -152,10 +180,9 @@ DLLM_DEV void row_scales(const GemvIn& in, float* red, float (&scale)[M]) {
   for (int m = 0; m < M; ++m) {
     scale[m] = 1.f;
     if (!in.norm_w || m >= in.m_rows) continue;
-    const float4* src = reinterpret_cast<const float4*>(in.x + (size_t)m * in.K);
     float ss = 0.f;
     for (int i = threadIdx.x; i < (in.K >> 2); i += blockDim.x) {
-      const float4 v = __ldcg(src + i);
+      const float4 v = load_in4(in, m, 4 * i);
       ss = fmaf(v.x, v.x, ss);
       ss = fmaf(v.y, v.y, ss);
       ss = fmaf(v.z, v.z, ss);
@@ -166,10 +193,14 @@ DLLM_DEV void row_scales(const GemvIn& in, float* red, float (&scale)[M]) {
   }
 }
 
-// Stage columns [k0, k1) of every row into xs[m * xstride + (k - k0)].
+// Stage columns [k0, k1) of every row into xs[m * xstride + (k - k0)]. With
+// in.save, the elements of this CTA's share of the rows (K split evenly over the
+// CTAs) are also written there, before normalisation.
 template <int M>
-DLLM_DEV void stage_x_block(const GemvIn& in, const float (&scale)[M], float* xs, int xstride, int k0, int k1) {
+DLLM_DEV void stage_x_block(const GemvIn& in, const float (&scale)[M], float* xs, int xstride, int k0, int k1,
+                            int cta, int ncta) {
   const int w4 = (k1 - k0) >> 2;
+  const int v0 = (int)(((long long)cta * in.K) / ncta), v1 = (int)(((long long)(cta + 1) * in.K) / ncta);
 #pragma unroll
   for (int m = 0; m < M; ++m) {
     float4* dst = reinterpret_cast<float4*>(xs + (size_t)m * xstride);
@@ -177,10 +208,17 @@ DLLM_DEV void stage_x_block(const GemvIn& in, const float (&scale)[M], float* xs
       for (int i = threadIdx.x; i < w4; i += blockDim.x) dst[i] = make_float4(0.f, 0.f, 0.f, 0.f);
       continue;
     }
-    const float4* src = reinterpret_cast<const float4*>(in.x + (size_t)m * in.K + k0);
     const uint2* g = in.norm_w ? reinterpret_cast<const uint2*>(in.norm_w + k0) : nullptr;
     for (int i = threadIdx.x; i < w4; i += blockDim.x) {
-      float4 v = __ldcg(src + i);
+      float4 v = load_in4(in, m, k0 + 4 * i);
+      const int e0 = k0 + 4 * i;
+      if (in.save && e0 + 3 >= v0 && e0 < v1) {
+        float* sv = in.save + (size_t)m * in.K;
+        const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (e0 + q >= v0 && e0 + q < v1) sv[e0 + q] = e[q];
+      }
       if (g) {
         const uint2 gg = __ldg(g + i);
         v.x = (v.x * scale[m]) * bf16_lo(gg.x);
@@ -192,6 +230,17 @@ DLLM_DEV void stage_x_block(const GemvIn& in, const float (&scale)[M], float* xs
     }
   }
   __syncthreads();
+}
+
+// in.save for a CTA without units in the phase: this CTA's share of every row.
+DLLM_DEV void save_share(const GemvIn& in, int cta, int ncta) {
+  const int v0 = (int)(((long long)cta * in.K) / ncta), v1 = (int)(((long long)(cta + 1) * in.K) / ncta);
+  for (int m = 0; m < in.m_rows; ++m)
+    for (int j = v0 + threadIdx.x; j < v1; j += blockDim.x) {
+      float v = __ldcg(in.x + (size_t)m * in.K + j);
+      if (in.acc) v = __fadd_rn(v, fix_to_f32(__ldcg(in.acc + j)));
+      in.save[(size_t)m * in.K + j] = v;
+    }
 }
 
 // Shared-memory budget a phase may use (floats).
@@ -241,7 +290,10 @@ DLLM_DEV void gemv_phase(const Epi& epi, const GemvIn& in, int units, const Phas
 
   float scale[M];
   row_scales<M>(in, sm.red, scale);
-  if (nu <= 0) return;
+  if (nu <= 0) {
+    if (in.save) save_share(in, cta, ncta);  // no staging here: write the share from L2
+    return;
+  }
 
   for (int b0 = 0; b0 < nu; b0 += ub) {
     const int nb = min(ub, nu - b0);
@@ -250,7 +302,7 @@ DLLM_DEV void gemv_phase(const Epi& epi, const GemvIn& in, int units, const Phas
       const int k0 = s0 * kSegElems, k1 = min(K, s1 * kSegElems);
       if (nblk > 1 || b0 == 0) {
         __syncthreads();  // previous readers of xs are done
-        stage_x_block<M>(in, scale, sm.xs, xstride, k0, k1);
+        stage_x_block<M>(in, scale, sm.xs, xstride, k0, k1, cta, ncta);
       }
       const int nsb = s1 - s0;
       const int ntask = nb * nsb;
@@ -358,19 +410,21 @@ struct EpiStore {
   DLLM_DEV void unit(int u, int m, const float* a, State&) const { y[(size_t)m * N + u] = a[0]; }
 };
 
-// h[m][j] = h[m][j] + x[m] . W[j]  (o_proj / down_proj then ctx.add, pipeline.js:66-67,73-74)
+// h[m][j] = src[m][j] + x[m] . W[j]  (o_proj / down_proj then ctx.add, pipeline.js:66-67,73-74);
+// src is h itself unless the residual was folded into a separate buffer.
 struct EpiResidual {
   static constexpr int R = 1;
   using State = NoState;
   const __nv_bfloat16* w;
   float* h;
   int N;
+  const float* src = nullptr;
   DLLM_DEV void unit_rows(int u, int K, const uint4** p) const {
     p[0] = reinterpret_cast<const uint4*>(w + (size_t)u * K);
   }
   DLLM_DEV void unit(int u, int m, const float* a, State&) const {
-    float* d = h + (size_t)m * N + u;
-    *d = __fadd_rn(__ldcg(d), a[0]);
+    const size_t i = (size_t)m * N + u;
+    h[i] = __fadd_rn(__ldcg((src ? src : h) + i), a[0]);
   }
 };
 
@@ -519,13 +573,15 @@ DLLM_DEV float transpose_reduce16(float (&v)[16]) {
   return v[0];
 }
 
-// This CTA's share of down_proj for one row: out[j] = sum over t < S of
+// This CTA's share of down_proj for one row: p[j] = sum over t < S of
 // Wd[j][k0 + t] * slice[t], for every output j < D, where slice is the CTA's own
-// SiLU(gate)*up values for columns [k0, k0 + S) (still in shared memory). Half-warp
+// SiLU(gate)*up values for columns [k0, k0 + S) (still in shared memory), added
+// to acc[j] in fixed point (f32_to_fix, one 64-bit atomic per output). Half-warp
 // = 16 lanes x 8 columns of one row; each lane keeps 16 rows' 16-byte weight
 // vectors in flight; the 16 row sums are transpose-reduced. S <= 128, k0 and the
 // row length I multiples of 8.
-DLLM_DEV void down_partial(const __nv_bfloat16* wd, int D, int I, int k0, int S, const float* slice, float* out) {
+DLLM_DEV void down_partial(const __nv_bfloat16* wd, int D, int I, int k0, int S, const float* slice,
+                           long long* acc) {
   constexpr int U = 16;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int cl = lane & 15, rsub = lane >> 4;
@@ -542,44 +598,35 @@ DLLM_DEV void down_partial(const __nv_bfloat16* wd, int D, int I, int k0, int S,
 #pragma unroll
     for (int u = 0; u < U; ++u)
       w[u] = (act && j0 + u < D) ? ld_stream16(wcol + (size_t)(j0 + u) * I) : make_uint4(0u, 0u, 0u, 0u);
-    float acc[U];
+    float acc_v[U];
 #pragma unroll
-    for (int u = 0; u < U; ++u) acc[u] = dot8(w[u], xa, xb, 0.f);
-    const float tot = transpose_reduce16(acc);  // lane cl: row j0 + cl
-    if (j0 + cl < D) out[j0 + cl] = tot;
+    for (int u = 0; u < U; ++u) acc_v[u] = dot8(w[u], xa, xb, 0.f);
+    const float tot = transpose_reduce16(acc_v);  // lane cl: row j0 + cl
+    if (j0 + cl < D) atomicAdd(reinterpret_cast<unsigned long long*>(acc + j0 + cl),
+                               static_cast<unsigned long long>(f32_to_fix(tot)));
   }
 }
 
-// down_proj result and residual for this CTA's rows: h[j] += sum over CTAs c
-// of part[c][j] (16 threads per row, each over c = g, g + 16, ...; the 16 sums
-// then added in order). red: >= blockDim.x floats of shared memory.
-DLLM_DEV void residual_reduce(const float* part, int D, int nparts, int cta, int ncta, float* h, float* red) {
+// The hidden row with the pending down_proj sums folded in, for this CTA's
+// share of the D elements: dst[j] = h[j] + acc[j] (the value load_in4 gives
+// every CTA), or h[j] when nothing is pending (acc null). With zero_acc the
+// share of acc is cleared (the next layer's sums start from zero).
+DLLM_DEV void fold_residual(const float* h, long long* acc, float* dst, int D, int cta, int ncta, bool zero_acc) {
   const int v0 = (int)(((long long)cta * D) / ncta), v1 = (int)(((long long)(cta + 1) * D) / ncta);
-  const int r = threadIdx.x >> 4, gq = threadIdx.x & 15;
-  const int rows_per = blockDim.x >> 4;
-  for (int rb = v0; rb < v1; rb += rows_per) {
-    const int j = rb + r;
-    float hv = 0.f;
-    if (gq == 0 && j < v1) hv = __ldcg(h + j);
-    float s = 0.f;
-    if (j < v1) {
-      for (int c0 = gq; c0 < nparts; c0 += 16 * 8) {
-        float v[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) v[q] = (c0 + 16 * q < nparts) ? __ldcg(part + (size_t)(c0 + 16 * q) * D + j) : 0.f;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) s += v[q];
-      }
+  for (int j = v0 + threadIdx.x; j < v1; j += blockDim.x) {
+    float v = __ldcg(h + j);
+    if (acc) {
+      v = __fadd_rn(v, fix_to_f32(__ldcg(acc + j)));
+      if (zero_acc) acc[j] = 0ll;
     }
-    red[threadIdx.x] = s;
-    __syncthreads();
-    if (gq == 0 && j < v1) {
-      float tot = 0.f;
-      for (int q = 0; q < 16; ++q) tot += red[r * 16 + q];
-      h[j] = __fadd_rn(hv, tot);
-    }
-    __syncthreads();
+    dst[j] = v;
   }
+}
+
+// Clear this CTA's share of the accumulator.
+DLLM_DEV void zero_share(long long* acc, int D, int cta, int ncta) {
+  const int v0 = (int)(((long long)cta * D) / ncta), v1 = (int)(((long long)(cta + 1) * D) / ncta);
+  for (int j = v0 + threadIdx.x; j < v1; j += blockDim.x) acc[j] = 0ll;
 }
 
 // ---- decode attention phase (ATTENTION, kernels.js:86-132) ------------------------------

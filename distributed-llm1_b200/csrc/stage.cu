@@ -16,9 +16,11 @@ cudaError_t configure_stage_kernels() {
 }
 
 // The split-K MLP (one row) needs 8-aligned column slices of down_proj of at
-// most 128 columns per CTA (16 lanes x 8), and a partials buffer.
+// most 128 columns per CTA (16 lanes x 8), and the accumulator after the
+// barrier counter.
 static bool splitk_fits(const StageParams& p, int grid) {
-  if (p.m_rows != 1 || !p.dpart || p.I % 8 != 0 || grid < 1) return false;
+  if (p.m_rows != 1 || !p.acc || !p.h2 || p.I % 8 != 0 || grid < 1) return false;
+  if (reinterpret_cast<const char*>(p.acc) != reinterpret_cast<const char*>(p.bar_count) + 16) return false;
   for (int c = 0; c < grid; ++c) {
     int u0 = (int)(((long long)c * p.I) / grid) / 8 * 8;
     int u1 = c + 1 == grid ? p.I : (int)(((long long)(c + 1) * p.I) / grid) / 8 * 8;
@@ -31,9 +33,11 @@ cudaError_t launch_stage(const StageParams& p0, int kv_dtype, int grid, cudaStre
   if (p0.m_rows < 1 || p0.m_rows > 8) return cudaErrorInvalidValue;
   StageParams p = p0;
   p.splitk = splitk_fits(p, grid) ? 1 : 0;
-  // the grid barrier's counter starts every launch at zero (a memset node when
-  // the launch is captured into a graph)
-  cudaError_t e = cudaMemsetAsync(p.bar_count, 0, sizeof(unsigned int), st);
+  // the grid barrier's counter (and, for the split-K MLP, the fixed-point
+  // accumulator right after it) starts every launch at zero: one memset node
+  // when the launch is captured into a graph
+  const size_t clear = p.splitk ? 16 + sizeof(long long) * (size_t)p.D : sizeof(unsigned int);
+  cudaError_t e = cudaMemsetAsync(p.bar_count, 0, clear, st);
   if (e != cudaSuccess) return e;
   return kv_dtype == 0 ? launch_stage_f32(p, grid, st) : launch_stage_bf16(p, grid, st);
 }

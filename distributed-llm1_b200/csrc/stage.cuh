@@ -66,7 +66,12 @@ struct StageParams {
   int32_t* out_tok;          // peer [m_rows]
   unsigned int* out_flag;    // peer
   unsigned int out_value;
-  float* dpart;              // split-K MLP: [grid][D] down_proj partials (one row)
+  // One-row split-K MLP: down_proj sums go into `acc` in fixed point (64-bit
+  // atomics) and are folded into the next phase's input instead of a reduction
+  // phase. acc must sit right after the barrier counter (bar_count + 4) so one
+  // memset clears both before every launch; h2 holds the folded row for o_proj.
+  long long* acc;            // [D]
+  float* h2;                 // [D]
   int splitk;                // use the split-K MLP (set by the host for one-row passes)
   int xs_floats;             // dynamic smem partition
   int part_floats;

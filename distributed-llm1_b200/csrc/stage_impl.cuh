@@ -12,6 +12,11 @@
 
 namespace dllm {
 
+DLLM_DEV AttnArgs attn_args(const StageParams& P, const LayerW& L) {
+  return AttnArgs{P.q, P.att, L.kc, L.vc, P.kv, P.rows, P.m_rows, P.NQ, P.KVH, P.scale, P.max_splits,
+                  P.part_o, P.part_ml, P.arrive, P.err};
+}
+
 template <typename KT, int HD, int M>
 __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P) {
   extern __shared__ __align__(16) float smem[];
@@ -61,73 +66,63 @@ __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P)
     trace();
   }
 
+  // One row with the split-K MLP: the down_proj sums of layer l wait in P.acc
+  // (fixed point) until layer l+1's QKV phase folds them into its input; the
+  // fold of this CTA's share also goes to P.h2, the residual o_proj adds to.
+  const bool fused = M == 1 && P.splitk;
   for (int l = 0; l < P.n_layers; ++l) {
     const LayerW L = P.layers[l];
+    const bool pending = fused && l > 0;  // layer l-1's down_proj sums
     // ---- QKV: rmsnorm -> q,k,v matmul -> addBias -> ropeQ/ropeK -> appendKv (pipeline.js:55-64)
     const EpiQKV<KT> eq{L.wq, L.wk, L.wv, L.bq, L.bk, L.bv, P.NQ, P.KVH, P.HD, P.log2_half, P.freq, P.q,
                         reinterpret_cast<KT*>(L.kc), reinterpret_cast<KT*>(L.vc), P.kv, P.rows, P.err};
-    gemv_phase<EpiQKV<KT>, M>(eq, GemvIn{P.h, D, P.m_rows, L.ln1, P.eps}, qkv_units, sm, cta, ncta, ns);
-    const EpiResidual eo{L.wo, P.h, D};
+    // (fused: the input is h + the pending sums; this CTA's share of it goes to h2)
+    gemv_phase<EpiQKV<KT>, M>(eq, GemvIn{P.h, D, P.m_rows, L.ln1, P.eps, pending ? P.acc : nullptr,
+                                         fused ? P.h2 : nullptr},
+                              qkv_units, sm, cta, ncta, ns);
+    const EpiResidual eo{L.wo, P.h, D, fused ? P.h2 : nullptr};
     prefetch_phase(eo, QD, D, cta, ncta, 2 * P.pref_bytes);
     if (!grid_barrier(P.bar_count, P.err)) return;
     trace();
 
     // ---- attention over slots [0, slot] (pipeline.js:65)
-    const AttnArgs A{P.q, P.att, L.kc, L.vc, P.kv, P.rows, P.m_rows, P.NQ, P.KVH, P.scale, P.max_splits,
-                     P.part_o, P.part_ml, P.arrive, P.err};
-    attn_phase<KT, HD>(A, smem, cta, ncta);
+    if (pending) zero_share(P.acc, D, cta, ncta);  // every CTA has read the sums
+    attn_phase<KT, HD>(attn_args(P, L), smem, cta, ncta);
     if (!grid_barrier(P.bar_count, P.err)) return;
     trace();
 
     // ---- o_proj + residual (pipeline.js:66-67)
     gemv_phase<EpiResidual, M>(eo, GemvIn{P.att, QD, P.m_rows, nullptr, 0.f}, D, sm, cta, ncta, ns);
     const EpiSiluGate eg{L.wg, L.wu, P.mid, P.I};
-    prefetch_phase(eg, D, P.I, cta, ncta, P.pref_bytes, M == 1 && P.splitk ? 8 : 1);  // the MLP's unit ranges
+    prefetch_phase(eg, D, P.I, cta, ncta, P.pref_bytes, fused ? 8 : 1);  // the MLP's unit ranges
     if (!grid_barrier(P.bar_count, P.err)) return;
     trace();
 
     // ---- rmsnorm -> gate, up -> siluMul (pipeline.js:69-72)
-    if (M == 1 && P.splitk) {
+    if (fused) {
       // Split-K MLP (one row): each CTA keeps its 8-aligned slice of SiLU(gate)*up
       // in shared memory and multiplies it straight into its column slice of
-      // down_proj for all rows (no barrier, no staging of the whole vector);
-      // the per-CTA partials are then summed per output row with the residual.
+      // down_proj for all rows (no barrier, no staging of the whole vector); the
+      // per-CTA partials go into P.acc, summed by integer atomics.
       int k0, k1;
       unit_range(P.I, cta, ncta, 8, k0, k1);
       float* slice = smem + P.xs_floats - 256;
       EpiSiluGate eg{L.wg, L.wu, P.mid, P.I, slice, k0};
       const PhaseSmem sm_g{smem, P.xs_floats - 256, sm.part, sm.part_floats, red};  // staging stops short of the slice
       gemv_phase<EpiSiluGate, M>(eg, GemvIn{P.h, D, P.m_rows, L.ln2, P.eps}, P.I, sm_g, cta, ncta, ns, 8);
-      // ---- down_proj (pipeline.js:73), this CTA's K-slice
-      down_partial(L.wd, D, P.I, k0, k1 - k0, slice, P.dpart + (size_t)cta * D);
-      // the next layer's first q|k|v rows (or the LM head) into L2 while the
-      // partials are reduced (issued before the barrier: measured 0.9 µs per
-      // layer faster than after the reduction)
-      if (l + 1 < P.n_layers) {
-        const LayerW Ln = P.layers[l + 1];
-        const EpiQKV<KT> en{Ln.wq, Ln.wk, Ln.wv, nullptr, nullptr, nullptr, P.NQ, P.KVH, P.HD, P.log2_half};
-        prefetch_phase(en, D, qkv_units, cta, ncta, P.pref_bytes);
-      } else if (P.lm_head) {
-        const EpiArgmax<M> ep{P.lm_head, P.V, nullptr};
-        prefetch_phase(ep, D, P.V, cta, ncta, P.pref_bytes);
-      }
+      // ---- down_proj (pipeline.js:73), this CTA's K-slice; + residual (:74) when folded
+      down_partial(L.wd, D, P.I, k0, k1 - k0, slice, P.acc);
+    } else {
+      gemv_phase<EpiSiluGate, M>(eg, GemvIn{P.h, D, P.m_rows, L.ln2, P.eps}, P.I, sm, cta, ncta, ns);
+      const EpiResidual ed{L.wd, P.h, D};
+      prefetch_phase(ed, P.I, D, cta, ncta, P.pref_bytes);
       if (!grid_barrier(P.bar_count, P.err)) return;
       trace();
-      // ---- + residual (pipeline.js:74): per-row sum of the partials
-      residual_reduce(P.dpart, D, ncta, cta, ncta, P.h, smem + P.xs_floats);
-      if (!grid_barrier(P.bar_count, P.err)) return;
-      trace();
-      continue;
-    }
-    // ---- rmsnorm -> gate, up -> siluMul (pipeline.js:69-72)
-    gemv_phase<EpiSiluGate, M>(eg, GemvIn{P.h, D, P.m_rows, L.ln2, P.eps}, P.I, sm, cta, ncta, ns);
-    const EpiResidual ed{L.wd, P.h, D};
-    prefetch_phase(ed, P.I, D, cta, ncta, P.pref_bytes);
-    if (!grid_barrier(P.bar_count, P.err)) return;
-    trace();
 
-    // ---- down_proj + residual (pipeline.js:73-74)
-    gemv_phase<EpiResidual, M>(ed, GemvIn{P.mid, P.I, P.m_rows, nullptr, 0.f}, D, sm, cta, ncta, ns);
+      // ---- down_proj + residual (pipeline.js:73-74)
+      gemv_phase<EpiResidual, M>(ed, GemvIn{P.mid, P.I, P.m_rows, nullptr, 0.f}, D, sm, cta, ncta, ns);
+    }
+    // the next layer's first q|k|v rows (or the LM head) into L2 across the barrier
     if (l + 1 < P.n_layers) {
       const LayerW Ln = P.layers[l + 1];
       const EpiQKV<KT> en{Ln.wq, Ln.wk, Ln.wv, nullptr, nullptr, nullptr, P.NQ, P.KVH, P.HD, P.log2_half};
@@ -136,6 +131,12 @@ __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P)
       const EpiArgmax<M> ep{P.lm_head, P.V, nullptr};
       prefetch_phase(ep, D, P.V, cta, ncta, P.pref_bytes);
     }
+    if (!grid_barrier(P.bar_count, P.err)) return;
+    trace();
+  }
+  if (fused && P.n_layers > 0) {
+    // ---- the last layer's down_proj sums + residual (pipeline.js:73-74) into h
+    fold_residual(P.h, P.acc, P.h, D, cta, ncta, true);
     if (!grid_barrier(P.bar_count, P.err)) return;
     trace();
   }
