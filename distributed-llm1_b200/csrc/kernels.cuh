@@ -576,15 +576,18 @@ DLLM_DEV float transpose_reduce16(float (&v)[16]) {
 // This CTA's share of down_proj for one row: p[j] = sum over t < S of
 // Wd[j][k0 + t] * slice[t], for every output j < D, where slice is the CTA's own
 // SiLU(gate)*up values for columns [k0, k0 + S) (still in shared memory), added
-// to acc[j] in fixed point (f32_to_fix, one 64-bit atomic per output). Half-warp
-// = 16 lanes x 8 columns of one row; each lane keeps 16 rows' 16-byte weight
-// vectors in flight; the 16 row sums are transpose-reduced. S <= 128, k0 and the
-// row length I multiples of 8.
+// to acc[j] in fixed point (f32_to_fix, one 64-bit atomic per output). A group of
+// LANES lanes (16: a half-warp, S <= 128; 32: the warp, S <= 256) covers the S
+// columns of a row, 8 per lane; each lane keeps 16 rows' 16-byte weight vectors
+// in flight; the 16 row sums are transpose-reduced. k0 and the row length I
+// multiples of 8.
+template <int LANES>
 DLLM_DEV void down_partial(const __nv_bfloat16* wd, int D, int I, int k0, int S, const float* slice,
                            long long* acc) {
   constexpr int U = 16;
+  constexpr int GROUPS = 32 / LANES;  // row groups per warp
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-  const int cl = lane & 15, rsub = lane >> 4;
+  const int cl = lane & (LANES - 1), rsub = lane / LANES;
   const bool act = cl * 8 < S;
   float4 xa = make_float4(0.f, 0.f, 0.f, 0.f), xb = xa;
   if (act) {
@@ -592,8 +595,8 @@ DLLM_DEV void down_partial(const __nv_bfloat16* wd, int D, int I, int k0, int S,
     xb = *reinterpret_cast<const float4*>(slice + cl * 8 + 4);
   }
   const __nv_bfloat16* wcol = wd + k0 + cl * 8;
-  for (int jb = 0; jb < D; jb += nwarps * 2 * U) {
-    const int j0 = jb + warp * 2 * U + rsub * U;  // this half-warp's 16 rows
+  for (int jb = 0; jb < D; jb += nwarps * GROUPS * U) {
+    const int j0 = jb + warp * GROUPS * U + rsub * U;  // this group's 16 rows
     uint4 w[U];
 #pragma unroll
     for (int u = 0; u < U; ++u)
@@ -601,9 +604,11 @@ DLLM_DEV void down_partial(const __nv_bfloat16* wd, int D, int I, int k0, int S,
     float acc_v[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) acc_v[u] = dot8(w[u], xa, xb, 0.f);
-    const float tot = transpose_reduce16(acc_v);  // lane cl: row j0 + cl
-    if (j0 + cl < D) atomicAdd(reinterpret_cast<unsigned long long*>(acc + j0 + cl),
-                               static_cast<unsigned long long>(f32_to_fix(tot)));
+    float tot = transpose_reduce16(acc_v);  // lane l of each half: row j0 + (l & 15), that half's columns
+    if (LANES == 32) tot += __shfl_xor_sync(0xffffffffu, tot, 16);
+    const int r = lane & 15;
+    if ((LANES == 16 || lane < 16) && j0 + r < D)
+      atomicAdd(reinterpret_cast<unsigned long long*>(acc + j0 + r), static_cast<unsigned long long>(f32_to_fix(tot)));
   }
 }
 

@@ -16,23 +16,27 @@ cudaError_t configure_stage_kernels() {
 }
 
 // The split-K MLP (one row) needs 8-aligned column slices of down_proj of at
-// most 128 columns per CTA (16 lanes x 8), and the accumulator after the
-// barrier counter.
-static bool splitk_fits(const StageParams& p, int grid) {
-  if (p.m_rows != 1 || !p.acc || !p.h2 || p.I % 8 != 0 || grid < 1) return false;
-  if (reinterpret_cast<const char*>(p.acc) != reinterpret_cast<const char*>(p.bar_count) + 16) return false;
+// most 128 columns per CTA (16 lanes x 8 per row group) or, with head_dim 128,
+// 256 (32 lanes x 8), and the accumulator after the barrier counter. Returns the
+// lanes per row group, or 0 when the pass cannot use it.
+static int splitk_lanes(const StageParams& p, int grid) {
+  if (p.m_rows != 1 || !p.acc || !p.h2 || p.I % 8 != 0 || grid < 1) return 0;
+  if (reinterpret_cast<const char*>(p.acc) != reinterpret_cast<const char*>(p.bar_count) + 16) return 0;
+  int widest = 0;
   for (int c = 0; c < grid; ++c) {
     int u0 = (int)(((long long)c * p.I) / grid) / 8 * 8;
     int u1 = c + 1 == grid ? p.I : (int)(((long long)(c + 1) * p.I) / grid) / 8 * 8;
-    if (u1 - u0 > 128) return false;
+    if (u1 - u0 > widest) widest = u1 - u0;
   }
-  return true;
+  if (widest <= 128) return 16;
+  if (widest <= 256 && p.HD == 128) return 32;
+  return 0;
 }
 
 cudaError_t launch_stage(const StageParams& p0, int kv_dtype, int grid, cudaStream_t st) {
   if (p0.m_rows < 1 || p0.m_rows > 8) return cudaErrorInvalidValue;
   StageParams p = p0;
-  p.splitk = splitk_fits(p, grid) ? 1 : 0;
+  p.splitk = splitk_lanes(p, grid);
   // the grid barrier's counter (and, for the split-K MLP, the fixed-point
   // accumulator right after it) starts every launch at zero: one memset node
   // when the launch is captured into a graph

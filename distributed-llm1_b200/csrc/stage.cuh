@@ -72,7 +72,7 @@ struct StageParams {
   // memset clears both before every launch; h2 holds the folded row for o_proj.
   long long* acc;            // [D]
   float* h2;                 // [D]
-  int splitk;                // use the split-K MLP (set by the host for one-row passes)
+  int splitk;                // split-K MLP lanes per row group (16 or 32; 0: off), set by launch_stage
   int xs_floats;             // dynamic smem partition
   int part_floats;
 };

@@ -17,7 +17,9 @@ DLLM_DEV AttnArgs attn_args(const StageParams& P, const LayerW& L) {
                   P.part_o, P.part_ml, P.arrive, P.err};
 }
 
-template <typename KT, int HD, int M>
+// SKL: lanes per row group of the split-K down projection (16: column slices of
+// up to 128, 32: up to 256; a separate instantiation, so each kernel carries one).
+template <typename KT, int HD, int M, int SKL = 16>
 __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P) {
   extern __shared__ __align__(16) float smem[];
   __shared__ float red[32];
@@ -111,7 +113,7 @@ __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P)
       const PhaseSmem sm_g{smem, P.xs_floats - 256, sm.part, sm.part_floats, red};  // staging stops short of the slice
       gemv_phase<EpiSiluGate, M>(eg, GemvIn{P.h, D, P.m_rows, L.ln2, P.eps}, P.I, sm_g, cta, ncta, ns, 8);
       // ---- down_proj (pipeline.js:73), this CTA's K-slice; + residual (:74) when folded
-      down_partial(L.wd, D, P.I, k0, k1 - k0, slice, P.acc);
+      down_partial<SKL>(L.wd, D, P.I, k0, k1 - k0, slice, P.acc);
     } else {
       gemv_phase<EpiSiluGate, M>(eg, GemvIn{P.h, D, P.m_rows, L.ln2, P.eps}, P.I, sm, cta, ncta, ns);
       const EpiResidual ed{L.wd, P.h, D};
@@ -205,9 +207,9 @@ __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P)
   }
 }
 
-template <typename KT, int HD, int M>
+template <typename KT, int HD, int M, int SKL = 16>
 static cudaError_t launch_one(const StageParams& p0, int grid, cudaStream_t st) {
-  auto fn = stage_kernel<KT, HD, M>;
+  auto fn = stage_kernel<KT, HD, M, SKL>;
   StageParams p = p0;
   if (M == 1 && p.splitk) {
     // One row with the split-K MLP: no phase stages more than a D- or
@@ -239,7 +241,11 @@ static cudaError_t launch_one(const StageParams& p0, int grid, cudaStream_t st) 
 
 template <typename KT, int HD>
 static cudaError_t launch_m(const StageParams& p, int grid, cudaStream_t st) {
-  if (p.m_rows <= 1) return launch_one<KT, HD, 1>(p, grid, st);
+  if (p.m_rows <= 1) {
+    if constexpr (HD == 128)
+      if (p.splitk == 32) return launch_one<KT, HD, 1, 32>(p, grid, st);
+    return launch_one<KT, HD, 1>(p, grid, st);
+  }
   if (p.m_rows <= 2) return launch_one<KT, HD, 2>(p, grid, st);
   if (p.m_rows <= 4) return launch_one<KT, HD, 4>(p, grid, st);
   return launch_one<KT, HD, 8>(p, grid, st);
@@ -252,6 +258,9 @@ static cudaError_t configure_hd() {
   if (e == cudaSuccess) e = cudaFuncSetAttribute(stage_kernel<KT, HD, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(stage_kernel<KT, HD, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(stage_kernel<KT, HD, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if constexpr (HD == 128)
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(stage_kernel<KT, HD, 1, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   return e;
 }
 

@@ -10,7 +10,10 @@ model widths, with fewer layers so the oracle finishes in seconds:
 * Qwen2.5-7B dims (28/4 heads, G = 7, MLP 18944, untied 152064-row LM head),
   2 layers, 2048 prefilled bf16 KV slots, 6 greedy steps;
 * Qwen2.5-1.5B dims (12/2 heads, G = 6, tied 151936-row head), 2 layers,
-  8192 prefilled slots, 4 steps.
+  8192 prefilled slots, 4 steps;
+* Qwen2.5-32B dims (40/8 heads, G = 5, MLP 27648: split-K column slices of up
+  to 192 columns, one warp per row group), 2 layers, 4096 prefilled slots,
+  3 steps.
 
 Weights are generated on the device and read back bit-exact; the prefilled KV
 is read back from the device cache, so the oracle (oracle/ref_forward.cpp in
@@ -36,6 +39,7 @@ pytestmark = pytest.mark.gpu
 CASES = {
     "7b": dict(preset="qwen2.5-7b", layers=2, kv_len=2048, steps=6),
     "1.5b": dict(preset="qwen2.5-1.5b", layers=2, kv_len=8192, steps=4),
+    "32b": dict(preset="qwen2.5-32b", layers=2, kv_len=4096, steps=3),
 }
 
 
