@@ -494,6 +494,8 @@ StageParams base_params(dllm_stage* s) {
   P.pref_bytes = kPrefetchBytes;
   P.trace = s->trace;
   P.trace_cap = s->trace_cap;
+  P.attn_kv_floats = (long long)f.max_pos * f.num_kv_heads > (long long)dllm::kAttnRingSlots * c->sms
+                         ? dllm::kAttnKvLongFloats : 0;
   P.xs_floats = dllm::kStageXsFloats;
   P.part_floats = dllm::kStagePartFloats;
   return P;

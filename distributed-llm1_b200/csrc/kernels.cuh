@@ -656,6 +656,7 @@ struct AttnArgs {
   float* part_ml;     // [M][NQ][max_splits][2]
   unsigned int* arrive;  // [2][m_rows][KVH] split arrivals then finishes, zero between uses
   int* err;
+  int kv_floats = 0;  // attn_item_ring: shared memory for the K/V ring (floats)
 };
 
 // Splits of a row's slots [0, T): each split is a multiple of 32 slots and is
@@ -675,12 +676,37 @@ DLLM_DEV int attn_splits(int T, int max_splits, int nsub, int* chunk_out) {
 
 // Slots of one K/V staging round of an attention item (a multiple of 32).
 constexpr int kAttnRound = 64;
+// attn_item_ring: rounds of 32 * cpr slots (cpr = 32-slot chunks per round, one
+// per sub-warp of a query head, at most 4) in a ring of up to kAttnMaxStages
+// rounds in shared memory, so later rounds' copies are in flight while one is
+// computed; the item's KV pages (up to kAttnPageTab) are looked up once.
+constexpr int kAttnMaxCpr = 4;
+constexpr int kAttnMaxStages = 4;
+constexpr int kAttnPageTab = 256;
 
-// Shared-memory floats attn_item needs: the K and V rows of one round, the
-// per-warp softmax state and partial outputs, and the split-merge scratch.
 template <typename KT, int HD>
-constexpr int attn_smem_floats() {
-  return (int)(2 * kAttnRound * HD * sizeof(KT) / sizeof(float)) + 2 * kWarps + kWarps * HD +
+__host__ __device__ constexpr int attn_round_floats(int cpr) {  // K and V rows of one round
+  return (int)(2 * 32 * cpr * HD * sizeof(KT) / sizeof(float));
+}
+template <typename KT, int HD>
+__host__ __device__ constexpr int attn_kv_default() {  // attn_item's single round
+  return attn_round_floats<KT, HD>(kAttnRound / 32);
+}
+// chunks per round and ring depth for `nsub` sub-warps per head within kv_floats
+template <typename KT, int HD>
+DLLM_DEV void attn_ring(int nsub, int kv_floats, int& cpr, int& nst) {
+  cpr = min(nsub, kAttnMaxCpr);
+  while (cpr > 1 && attn_round_floats<KT, HD>(cpr) > kv_floats) --cpr;
+  nst = kv_floats / attn_round_floats<KT, HD>(cpr);
+  nst = max(1, min(kAttnMaxStages, nst));
+}
+
+// Shared-memory floats the attention of an item needs: the K/V rows (one round,
+// or the ring of kv_floats), the per-warp softmax state and partial outputs, and
+// the split-merge scratch.
+template <typename KT, int HD>
+__host__ __device__ constexpr int attn_smem_floats(int kv_floats = 0) {
+  return (kv_floats > 0 ? kv_floats : attn_kv_default<KT, HD>()) + 2 * kWarps + kWarps * HD +
          2 * kGMax * kAttnMaxSplits + kGMax + 32 * 16;
 }
 
@@ -692,6 +718,16 @@ DLLM_DEV void cp_async16(void* smem_dst, const void* gsrc) {
                : "memory");
 }
 DLLM_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+DLLM_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Wait until at most `pending` of this thread's committed groups are incomplete.
+DLLM_DEV void cp_async_wait_pending(int pending) {
+  switch (pending) {
+    case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
+    case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
+    case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
+    default: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+  }
+}
 
 // DPL consecutive KV elements (shared memory) -> fp32.
 template <typename KT, int DPL>
@@ -982,8 +1018,145 @@ DLLM_DEV void attn_item(const AttnArgs& A, int m, int g, int s, int nsplit, int 
   attn_finish<HD>(A, m, g, s, nsplit, G, min(nsub, CPR), wm, wl, wacc, mrg);
 }
 
-// All attention work items of a pass, spread round-robin over the CTAs.
+// attn_item for long contexts, staging K/V through a ring of A.kv_floats of
+// shared memory: the item's slots are taken in rounds of 32 * cpr slots, copied
+// (cp.async, each row read once for all G query heads) nst - 1 rounds ahead of
+// the round being computed, so HBM latency overlaps the q.k / p.V work. The
+// item's KV pages are looked up once (page_base), so a copy needs no dependent
+// load. Per round the math is attn_item's: warp w = c*G + h computes query head
+// h over the round's 32-slot chunk c.
 template <typename KT, int HD>
+DLLM_DEV void attn_item_ring(const AttnArgs& A, int m, int g, int s, int nsplit, int chunk, float* smem) {
+  constexpr int DPL = HD / 32;
+  constexpr int VPR = HD * (int)sizeof(KT) / 16;  // 16-byte vectors per K or V row
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int G = A.NQ / A.KVH;
+  const int nsub = max(1, kWarps / G);
+  const int h = warp % G, c = warp / G;
+  const int kvf = A.kv_floats;
+  int cpr, nst;
+  attn_ring<KT, HD>(nsub, kvf, cpr, nst);
+  const int R = 32 * cpr;  // slots per round
+  const bool active = c < min(nsub, cpr);
+  const RowDesc rd = A.rows[m];
+  const int T = rd.slot + 1;
+  const int p0 = s * chunk, p1 = min(T, p0 + chunk);
+  KT* ring = reinterpret_cast<KT*>(smem);      // per stage: [R][HD] K rows, then [R][HD] V rows
+  float* wm = smem + kvf;                      // [kWarps]
+  float* wl = wm + kWarps;                     // [kWarps]
+  float* wacc = wl + kWarps;                   // [kWarps][HD]
+  float* mrg = wacc + kWarps * HD;             // split merge scratch
+  const KT* kc = reinterpret_cast<const KT*>(A.kc);
+  const KT* vc = reinterpret_cast<const KT*>(A.vc);
+
+  float q[DPL];
+  if (active) {
+    const float* qh = A.q + (size_t)m * A.NQ * HD + (size_t)(g * G + h) * HD + lane * DPL;
+#pragma unroll
+    for (int d = 0; d < DPL; ++d) q[d] = __ldcg(qh + d);
+  }
+  float mrun = -INFINITY, lsum = 0.f, acc[DPL];
+#pragma unroll
+  for (int d = 0; d < DPL; ++d) acc[d] = 0.f;
+
+  // the item's pages: page_base[p] = element offset of slot 0 of logical page
+  // lp0 + p for head g (in the split-merge scratch, free until attn_finish)
+  long long* page_base = reinterpret_cast<long long*>(mrg);
+  const int lp0 = p0 >> A.kv.log2_page;
+  const int npg = p1 > p0 ? ((p1 - 1) >> A.kv.log2_page) - lp0 + 1 : 0;
+  const bool tab = npg <= kAttnPageTab;
+  if (tab && (int)threadIdx.x < npg)
+    page_base[threadIdx.x] = A.kv.offset(rd.seq, (lp0 + (int)threadIdx.x) << A.kv.log2_page, g);
+  __syncthreads();
+  const int nr = (p1 - p0 + R - 1) / R;
+  // copies of round r into its ring stage; a 32-slot chunk lies in one KV page
+  auto issue = [&](int r) {
+    const int base = p0 + r * R;
+    const int n = min(R, p1 - base);
+    KT* ks = ring + (size_t)(r % nst) * 2 * R * HD;
+    KT* vs = ks + R * HD;
+    const int nvec = ((n + 31) >> 5) * 32 * VPR;  // per K or V
+    for (int i = threadIdx.x; i < 2 * nvec; i += blockDim.x) {
+      const int which = i >= nvec;
+      const int rr = which ? i - nvec : i;
+      const int j = rr / VPR, v = rr - j * VPR;
+      const int slot = base + j;
+      if (slot >= p1) continue;
+      const long long off =
+          tab ? page_base[(slot >> A.kv.log2_page) - lp0] +
+                    (long long)(slot & ((1 << A.kv.log2_page) - 1)) * A.kv.row_stride
+              : A.kv.offset(rd.seq, base + (j & ~31), g) + (long long)(j & 31) * A.kv.row_stride;
+      const KT* src = (which ? vc : kc) + off + v * (16 / (int)sizeof(KT));
+      KT* dst = (which ? vs : ks) + j * HD + v * (16 / (int)sizeof(KT));
+      cp_async16(dst, src);
+    }
+  };
+  for (int r = 0; r < nst - 1; ++r) {
+    if (r < nr) issue(r);
+    cp_async_commit();
+  }
+  for (int r = 0; r < nr; ++r) {
+    __syncthreads();  // readers of round r - 1 (whose stage round r + nst - 1 reuses) are done
+    if (r + nst - 1 < nr) issue(r + nst - 1);
+    cp_async_commit();
+    cp_async_wait_pending(nst - 1);  // this thread's copies of round r have landed
+    __syncthreads();                 // and every thread's
+    const int n = min(R, p1 - (p0 + r * R));
+    const KT* ks = ring + (size_t)(r % nst) * 2 * R * HD;
+    const KT* vs = ks + R * HD;
+    if (active) {
+      for (int cc = c; cc * 32 < n; cc += nsub) {
+        const int nvalid = min(32, n - cc * 32);
+        const KT* kr = ks + (cc * 32) * HD + lane * DPL;
+        const KT* vr = vs + (cc * 32) * HD + lane * DPL;
+        float part[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float kv[DPL];
+          kv_row_part<KT, DPL>(kr + j * HD, kv);
+          float sdot = 0.f;
+#pragma unroll
+          for (int d = 0; d < DPL; ++d) sdot = fmaf(q[d], kv[d], sdot);
+          part[j] = sdot;
+        }
+        const float sc = transpose_reduce32(part);  // lane = slot in the chunk
+        const bool valid = lane < nvalid;
+        const float sv = valid ? __fmul_rn(sc, A.scale) : -INFINITY;
+        const float mnew = fmaxf(mrun, warp_max(sv));
+        const float alpha = (mrun == -INFINITY) ? 0.f : expf(mrun - mnew);
+        const float pv = valid ? expf(sv - mnew) : 0.f;
+        lsum = fmaf(lsum, alpha, pv);
+        mrun = mnew;
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) acc[d] *= alpha;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float pj = __shfl_sync(0xffffffffu, pv, j);
+          if (j < nvalid) {  // rows past the item were not copied
+            float vv[DPL];
+            kv_row_part<KT, DPL>(vr + j * HD, vv);
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) acc[d] = fmaf(pj, vv[d], acc[d]);
+          }
+        }
+      }
+    }
+  }
+  cp_async_wait_pending(0);  // nothing in flight leaves the item (only empty groups remain)
+  const float l = warp_sum(lsum);
+  if (lane == 0) {
+    wm[warp] = active ? mrun : -INFINITY;
+    wl[warp] = active ? l : 0.f;
+  }
+#pragma unroll
+  for (int d = 0; d < DPL; ++d) wacc[warp * HD + lane * DPL + d] = active ? acc[d] : 0.f;
+  __syncthreads();
+  attn_finish<HD>(A, m, g, s, nsplit, G, min(nsub, cpr), wm, wl, wacc, mrg);
+}
+
+// All attention work items of a pass, spread round-robin over the CTAs.
+// RING: items go through attn_item_ring (A.kv_floats of shared memory).
+template <typename KT, int HD, bool RING = false>
 DLLM_DEV void attn_phase(const AttnArgs& A, float* smem, int cta, int ncta) {
   // enumerate items: rows in order, kv heads, splits
   int item = 0;
@@ -1003,7 +1176,8 @@ DLLM_DEV void attn_phase(const AttnArgs& A, float* smem, int cta, int ncta) {
     if (j0 < 0) j0 += ncta;
     for (int j = j0; j < n_items; j += ncta) {
       const int g = j / ns, s = j - g * ns;
-      attn_item<KT, HD>(A, m, g, s, ns, chunk, smem);
+      if constexpr (RING) attn_item_ring<KT, HD>(A, m, g, s, ns, chunk, smem);
+      else attn_item<KT, HD>(A, m, g, s, ns, chunk, smem);
     }
     item += n_items;
   }

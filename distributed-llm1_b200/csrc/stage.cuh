@@ -73,6 +73,7 @@ struct StageParams {
   long long* acc;            // [D]
   float* h2;                 // [D]
   int splitk;                // split-K MLP lanes per row group (16 or 32; 0: off), set by launch_stage
+  int attn_kv_floats;        // attention K/V ring in shared memory (floats; 0: one round at a time)
   int xs_floats;             // dynamic smem partition
   int part_floats;
 };
@@ -82,6 +83,13 @@ constexpr int kStageXsFloats = 32768;    // 128 KB of staged activations
 constexpr int kStagePartFloats = 16384;  // 64 KB of segment partials
 constexpr int kStageSmallPartFloats = 4096;  // 16 KB: the one-row split-K partition
 constexpr size_t kStageSmemBytes = (size_t)(kStageXsFloats + kStagePartFloats) * sizeof(float);
+// Attention K/V ring: 144 KB, i.e. up to 3-4 rounds in flight while one is
+// computed, for stages whose attention items can hold more than kAttnRingSlots
+// slots on average (max_pos * KV heads / SMs): long items make attention a large
+// share of the pass; short ones (a round or two each) keep one round at a time
+// and leave the shared memory to L1, which the weight streaming needs more.
+constexpr int kAttnRingSlots = 256;
+constexpr int kAttnKvLongFloats = 36864;
 
 // Launches stage_kernel<KT, HD, M> with M the smallest of {1,2,4,8} >= m_rows,
 // one CTA per SM, cooperative (all CTAs resident). kv_dtype: 0 fp32, 1 bf16.

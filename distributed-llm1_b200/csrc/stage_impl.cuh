@@ -14,12 +14,14 @@ namespace dllm {
 
 DLLM_DEV AttnArgs attn_args(const StageParams& P, const LayerW& L) {
   return AttnArgs{P.q, P.att, L.kc, L.vc, P.kv, P.rows, P.m_rows, P.NQ, P.KVH, P.scale, P.max_splits,
-                  P.part_o, P.part_ml, P.arrive, P.err};
+                  P.part_o, P.part_ml, P.arrive, P.err, P.attn_kv_floats};
 }
 
 // SKL: lanes per row group of the split-K down projection (16: column slices of
-// up to 128, 32: up to 256; a separate instantiation, so each kernel carries one).
-template <typename KT, int HD, int M, int SKL = 16>
+// up to 128, 32: up to 256). RING: attention K/V staged through the multi-round
+// ring (P.attn_kv_floats > 0, long contexts). Separate instantiations, so each
+// kernel carries one variant of each.
+template <typename KT, int HD, int M, int SKL = 16, bool RING = false>
 __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P) {
   extern __shared__ __align__(16) float smem[];
   __shared__ float red[32];
@@ -89,7 +91,7 @@ __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P)
 
     // ---- attention over slots [0, slot] (pipeline.js:65)
     if (pending) zero_share(P.acc, D, cta, ncta);  // every CTA has read the sums
-    attn_phase<KT, HD>(attn_args(P, L), smem, cta, ncta);
+    attn_phase<KT, HD, RING>(attn_args(P, L), smem, cta, ncta);
     if (!grid_barrier(P.bar_count, P.err)) return;
     trace();
 
@@ -207,9 +209,9 @@ __global__ void __launch_bounds__(kThreads, 1) stage_kernel(const StageParams P)
   }
 }
 
-template <typename KT, int HD, int M, int SKL = 16>
+template <typename KT, int HD, int M, int SKL = 16, bool RING = false>
 static cudaError_t launch_one(const StageParams& p0, int grid, cudaStream_t st) {
-  auto fn = stage_kernel<KT, HD, M, SKL>;
+  auto fn = stage_kernel<KT, HD, M, SKL, RING>;
   StageParams p = p0;
   if (M == 1 && p.splitk) {
     // One row with the split-K MLP: no phase stages more than a D- or
@@ -219,7 +221,8 @@ static cudaError_t launch_one(const StageParams& p0, int grid, cudaStream_t st) 
     const int K = p.D > p.NQ * p.HD ? p.D : p.NQ * p.HD;
     int xs = ((K + 4095) / 4096) * 4096 + 256;  // staged x + the SiLU(gate)*up slice
     const int part = kStageSmallPartFloats;
-    if (xs + part < attn_smem_floats<KT, HD>()) xs = attn_smem_floats<KT, HD>() - part;
+    const int attn = attn_smem_floats<KT, HD>(RING ? p.attn_kv_floats : 0);
+    if (xs + part < attn) xs = attn - part;
     xs = (xs + 3) & ~3;  // 16-byte aligned partial and slice areas
     if (xs + part < kStageXsFloats + kStagePartFloats) {
       p.xs_floats = xs;
@@ -239,28 +242,41 @@ static cudaError_t launch_one(const StageParams& p0, int grid, cudaStream_t st) 
   return cudaLaunchKernelEx(&cfg, fn, p);
 }
 
-template <typename KT, int HD>
-static cudaError_t launch_m(const StageParams& p, int grid, cudaStream_t st) {
+template <typename KT, int HD, bool RING>
+static cudaError_t launch_m_ring(const StageParams& p, int grid, cudaStream_t st) {
   if (p.m_rows <= 1) {
     if constexpr (HD == 128)
-      if (p.splitk == 32) return launch_one<KT, HD, 1, 32>(p, grid, st);
-    return launch_one<KT, HD, 1>(p, grid, st);
+      if (p.splitk == 32) return launch_one<KT, HD, 1, 32, RING>(p, grid, st);
+    return launch_one<KT, HD, 1, 16, RING>(p, grid, st);
   }
-  if (p.m_rows <= 2) return launch_one<KT, HD, 2>(p, grid, st);
-  if (p.m_rows <= 4) return launch_one<KT, HD, 4>(p, grid, st);
-  return launch_one<KT, HD, 8>(p, grid, st);
+  if (p.m_rows <= 2) return launch_one<KT, HD, 2, 16, RING>(p, grid, st);
+  if (p.m_rows <= 4) return launch_one<KT, HD, 4, 16, RING>(p, grid, st);
+  return launch_one<KT, HD, 8, 16, RING>(p, grid, st);
+}
+
+template <typename KT, int HD>
+static cudaError_t launch_m(const StageParams& p, int grid, cudaStream_t st) {
+  if (p.attn_kv_floats > 0) return launch_m_ring<KT, HD, true>(p, grid, st);
+  return launch_m_ring<KT, HD, false>(p, grid, st);
+}
+
+template <typename KT, int HD, bool RING>
+static cudaError_t configure_ring() {
+  const int bytes = (int)kStageSmemBytes;
+  cudaError_t e = cudaFuncSetAttribute(stage_kernel<KT, HD, 1, 16, RING>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(stage_kernel<KT, HD, 2, 16, RING>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(stage_kernel<KT, HD, 4, 16, RING>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(stage_kernel<KT, HD, 8, 16, RING>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if constexpr (HD == 128)
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(stage_kernel<KT, HD, 1, 32, RING>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  return e;
 }
 
 template <typename KT, int HD>
 static cudaError_t configure_hd() {
-  const int bytes = (int)kStageSmemBytes;
-  cudaError_t e = cudaFuncSetAttribute(stage_kernel<KT, HD, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(stage_kernel<KT, HD, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(stage_kernel<KT, HD, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(stage_kernel<KT, HD, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if constexpr (HD == 128)
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(stage_kernel<KT, HD, 1, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  cudaError_t e = configure_ring<KT, HD, false>();
+  if (e == cudaSuccess) e = configure_ring<KT, HD, true>();
   return e;
 }
 

@@ -94,15 +94,21 @@ def test_benched_decode_matches_oracle(dllm, case):
     ctx.close()
 
 
-@pytest.mark.parametrize("preset,T", [("qwen2.5-7b", 1024), ("qwen2.5-7b", 4096), ("qwen2.5-7b", 16384),
-                                      ("qwen2.5-7b", 32768), ("qwen2.5-32b", 32768)])
-def test_paged_bf16_attention_matches_oracle(dllm, preset, T):
-    """One decode row at position T over T prefilled bf16 slots plus its own: the
+@pytest.mark.parametrize("preset,T,kv", [("qwen2.5-7b", 1024, "bf16"), ("qwen2.5-7b", 4096, "bf16"),
+                                         ("qwen2.5-7b", 16384, "bf16"), ("qwen2.5-7b", 32768, "bf16"),
+                                         ("qwen2.5-32b", 32768, "bf16"), ("qwen2.5-1.5b", 8192, "bf16"),
+                                         ("qwen2.5-7b", 16384, "f32"), ("qwen2.5-32b", 5000, "f32")])
+def test_paged_attention_matches_oracle(dllm, preset, T, kv):
+    """One decode row at position T over T prefilled slots plus its own: the
     attention output of the stage kernel equals the oracle's attention
-    (kernels.js:86-132) on the same q and the same cache contents."""
+    (kernels.js:86-132) on the same q and the same cache contents. Stages whose
+    attention items average more than 256 slots (max_pos * KV heads / SMs: here
+    7B from 16k, 32B from 5k) stage K/V through the multi-round ring (rounds of
+    64 slots at G = 7, 96 at G = 5; up to 4 rounds in flight for bf16, 2 for
+    f32), the others one round at a time."""
     import ctypes as C
     syn = importlib.import_module("distributed-llm1_b200.synthetic")
-    cfg = dllm.PRESETS[preset].with_(num_layers=1, kv_dtype="bf16", max_pos=T + 64)
+    cfg = dllm.PRESETS[preset].with_(num_layers=1, kv_dtype=kv, max_pos=T + 64)
     ctx = dllm.initKernels(0, cfg)
     st = dllm.Stage(ctx, 0, 1)
     syn.device_weights(ctx, st, cfg, 0, 1, embed=False, head=False, seed=T)
@@ -117,6 +123,6 @@ def test_paged_bf16_attention_matches_oracle(dllm, preset, T):
     F = C.POINTER(C.c_float)
     ref_lib().ref_attention(q.ctypes.data_as(F), K.ctypes.data_as(F), V.ctypes.data_as(F), out.ctypes.data_as(F),
                             T, 1, cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim)
-    assert_close(att, out, rtol=1e-3, atol=1e-4, what=f"{preset} attention T={T}")
+    assert_close(att, out, rtol=1e-3, atol=1e-4, what=f"{preset} {kv} attention T={T}")
     st.close()
     ctx.close()
