@@ -8,9 +8,11 @@ in flight. Workload (Qwen2.5-7B architecture, random-init bf16 weights, 2048-slo
 synthetic N(0,1) bf16 KV prefill per sequence):
   * N=1: batch 1 through the whole model on one GPU; one persistent stage-kernel
     launch per token, replayed as a CUDA graph with the token kept on device.
-  * N>1: contiguous layer stages, one per GPU (plan_stages), N sequences in
-    flight as micro-batches, hidden rows hopped to the next GPU with NCCL
-    send/recv (multigpu.py). Per-GPU work per step is fixed: weak scaling.
+  * N>1: contiguous layer stages, one per GPU (plan_stages), N micro-batches
+    of --micro sequences in flight; the hidden-row hop is fused into the stage
+    kernel (16-byte stores into the next GPU's receive buffer over NVLink and a
+    released flag; dllm_pipeline_* through multigpu.NvlinkRing). Per-GPU work
+    per step is fixed: weak scaling.
 `value` is tokens/s of the whole job timed with CUDA events on the launching
 stream (max over ranks); `e2e` is the same metric through the public generate
 call with the token copied host->device and back every step. Weights (15 GB)

@@ -921,7 +921,8 @@ DLLM_DEV void attn_finish(const AttnArgs& A, int m, int g, int s, int nsplit, in
 // so lane p holds slot p's score; online softmax per warp; p.V: lane l
 // accumulates its dims. Chunk groups of a head are combined in attn_finish.
 template <typename KT, int HD>
-DLLM_DEV void attn_item(const AttnArgs& A, int m, int g, int s, int nsplit, int chunk, float* smem) {
+DLLM_DEV void attn_item(const AttnArgs& A, int m, int g, int s, int nsplit, int chunk, float* smem,
+                        int skip = 0) {
   constexpr int DPL = HD / 32;
   constexpr int VPR = HD * (int)sizeof(KT) / 16;  // 16-byte vectors per K or V row
   constexpr int CPR = kAttnRound / 32;           // 32-slot chunks per round
@@ -961,7 +962,7 @@ DLLM_DEV void attn_item(const AttnArgs& A, int m, int g, int s, int nsplit, int 
       const int which = i >= nvec;
       const int r = which ? i - nvec : i;
       const int j = r / VPR, v = r - j * VPR;
-      if (base + j >= p1) continue;
+      if (base + j >= p1 || (base == p0 && j < skip)) continue;  // rows [p0, p0 + skip) are in flight already
       const long long off = A.kv.offset(rd.seq, base + (j & ~31), g) + (long long)(j & 31) * A.kv.row_stride;
       const KT* src = (which ? vc : kc) + off + v * (16 / (int)sizeof(KT));
       KT* dst = (which ? vs : ks) + j * HD + v * (16 / (int)sizeof(KT));
@@ -1026,7 +1027,8 @@ DLLM_DEV void attn_item(const AttnArgs& A, int m, int g, int s, int nsplit, int 
 // load. Per round the math is attn_item's: warp w = c*G + h computes query head
 // h over the round's 32-slot chunk c.
 template <typename KT, int HD>
-DLLM_DEV void attn_item_ring(const AttnArgs& A, int m, int g, int s, int nsplit, int chunk, float* smem) {
+DLLM_DEV void attn_item_ring(const AttnArgs& A, int m, int g, int s, int nsplit, int chunk, float* smem,
+                             int skip = 0) {
   constexpr int DPL = HD / 32;
   constexpr int VPR = HD * (int)sizeof(KT) / 16;  // 16-byte vectors per K or V row
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -1081,7 +1083,7 @@ DLLM_DEV void attn_item_ring(const AttnArgs& A, int m, int g, int s, int nsplit,
       const int rr = which ? i - nvec : i;
       const int j = rr / VPR, v = rr - j * VPR;
       const int slot = base + j;
-      if (slot >= p1) continue;
+      if (slot >= p1 || (r == 0 && j < skip)) continue;  // rows [p0, p0 + skip) are in flight already
       const long long off =
           tab ? page_base[(slot >> A.kv.log2_page) - lp0] +
                     (long long)(slot & ((1 << A.kv.log2_page) - 1)) * A.kv.row_stride
@@ -1154,12 +1156,77 @@ DLLM_DEV void attn_item_ring(const AttnArgs& A, int m, int g, int s, int nsplit,
   attn_finish<HD>(A, m, g, s, nsplit, G, min(nsub, cpr), wm, wl, wacc, mrg);
 }
 
+// One-row passes: the rows of the first staging round of this CTA's first
+// attention item that exist before the pass (every slot but the one the pass
+// appends), located once per launch (the rows and page table do not change
+// during it; the layer only changes the pool base). attn_early_issue copies them
+// into the round's place in shared memory at the end of the QKV phase, so they
+// land while the grid barrier completes; attn_phase then copies the rest.
+struct AttnEarly {
+  int n;              // rows to copy ahead (0: none)
+  int R;              // rows of the item's first round (its stage-0 layout)
+  long long coff[kAttnMaxCpr];  // element offset of each 32-slot chunk (head g)
+};
+
+template <typename KT, int HD, bool RING>
+DLLM_DEV void attn_early_plan(const AttnArgs& A, int cta, int ncta, AttnEarly* plan) {
+  if (threadIdx.x == 0) {
+    plan->n = 0;
+    const RowDesc rd = A.rows[0];
+    if (A.m_rows == 1 && rd.slot >= 0 && rd.slot < A.kv.max_slots && rd.seq >= 0 && rd.seq < A.kv.num_seqs) {
+      const int nsub = max(1, kWarps / (A.NQ / A.KVH));
+      int chunk;
+      const int ns = attn_splits(rd.slot + 1, A.max_splits, nsub, &chunk);
+      if (cta < A.KVH * ns) {
+        const int g = cta / ns, sp = cta - g * ns;
+        int R = kAttnRound;
+        if (RING) {
+          int cpr, nst;
+          attn_ring<KT, HD>(nsub, A.kv_floats, cpr, nst);
+          R = 32 * cpr;
+        }
+        const int p0 = sp * chunk;
+        const int n = min(R, min(rd.slot, p0 + chunk) - p0);  // rows before the appended slot
+        if (n > 0) {
+          plan->R = R;
+          for (int c = 0; c * 32 < n; ++c) plan->coff[c] = A.kv.offset(rd.seq, p0 + 32 * c, g);
+          plan->n = n;
+        }
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// Issue the planned copies into shared memory (one cp.async group) for this layer's pools.
+template <typename KT, int HD>
+DLLM_DEV int attn_early_issue(const AttnEarly& plan, const void* kc_, const void* vc_, int row_stride, float* smem) {
+  constexpr int VPR = HD * (int)sizeof(KT) / 16;
+  const int n = plan.n;
+  if (n <= 0) return 0;
+  const KT* kc = reinterpret_cast<const KT*>(kc_);
+  const KT* vc = reinterpret_cast<const KT*>(vc_);
+  KT* ks = reinterpret_cast<KT*>(smem);
+  KT* vs = ks + plan.R * HD;
+  const int nvec = n * VPR;
+  for (int i = threadIdx.x; i < 2 * nvec; i += blockDim.x) {
+    const int which = i >= nvec;
+    const int r = which ? i - nvec : i;
+    const int j = r / VPR, v = r - j * VPR;
+    const long long off = plan.coff[j >> 5] + (long long)(j & 31) * row_stride;
+    cp_async16((which ? vs : ks) + j * HD + v * (16 / (int)sizeof(KT)), (which ? vc : kc) + off + v * (16 / (int)sizeof(KT)));
+  }
+  cp_async_commit();
+  return n;
+}
+
 // All attention work items of a pass, spread round-robin over the CTAs.
 // RING: items go through attn_item_ring (A.kv_floats of shared memory).
 template <typename KT, int HD, bool RING = false>
-DLLM_DEV void attn_phase(const AttnArgs& A, float* smem, int cta, int ncta) {
+DLLM_DEV void attn_phase(const AttnArgs& A, float* smem, int cta, int ncta, int first_skip = 0) {
   // enumerate items: rows in order, kv heads, splits
   int item = 0;
+  int skip = first_skip;  // rows of this CTA's first item issued ahead (attn_early_issue)
   for (int m = 0; m < A.m_rows; ++m) {
     const RowDesc rd = A.rows[m];
     if (rd.slot < 0 || rd.slot >= A.kv.max_slots || rd.seq < 0 || rd.seq >= A.kv.num_seqs) {
@@ -1176,8 +1243,9 @@ DLLM_DEV void attn_phase(const AttnArgs& A, float* smem, int cta, int ncta) {
     if (j0 < 0) j0 += ncta;
     for (int j = j0; j < n_items; j += ncta) {
       const int g = j / ns, s = j - g * ns;
-      if constexpr (RING) attn_item_ring<KT, HD>(A, m, g, s, ns, chunk, smem);
-      else attn_item<KT, HD>(A, m, g, s, ns, chunk, smem);
+      if constexpr (RING) attn_item_ring<KT, HD>(A, m, g, s, ns, chunk, smem, skip);
+      else attn_item<KT, HD>(A, m, g, s, ns, chunk, smem, skip);
+      skip = 0;
     }
     item += n_items;
   }
