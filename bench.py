@@ -62,6 +62,10 @@ def parse_args():
                    choices=["all", "matvec", "gemm", "attention", "norm"],
                    help="isolated kernel sweep (matvec / tensor-core GEMM shapes, attention lengths, RMSNorm and "
                         "RoPE at hidden 3584): one JSON line per case instead of the decode benchmark")
+    p.add_argument("--phase-trace", action="store_true",
+                   help="per-phase time of the persistent stage kernel (global-timer stamps of CTA 0 after every "
+                        "grid barrier) with each phase's algorithmic bytes and fraction of the measured HBM peak: "
+                        "one JSON line instead of the decode benchmark")
     p.add_argument("--layers", type=int, default=0,
                    help="profiling case only: run the first N layers + LM head (a few GB on the device); "
                         "the line is marked and is not the benchmark")
@@ -81,7 +85,7 @@ def measured_peaks() -> tuple[float, str]:
 # 7B decode launch (2 layers + LM head, 2048-slot bf16 KV) over that launch's
 # weight + KV + embedding bytes. Re-measure with the profiling command when the
 # kernel changes.
-STAGE_TRAFFIC_RATIO = 1.0022
+STAGE_TRAFFIC_RATIO = 1.0028
 
 
 def traffic_bytes(algorithmic: float, model: str) -> float | None:
@@ -512,10 +516,74 @@ def run_kernel_sweep(args):
     return lines
 
 
+# ---- per-phase trace of the stage kernel ------------------------------------------------------
+PHASES = ["qkv", "attention", "o_proj", "mlp"]
+
+
+def run_phase_trace(args, tokens: int = 5):
+    """Decode `tokens` single tokens with the stage kernel's global-timer trace on
+    (CTA 0 stamps kernel start and every grid barrier) and report the median time
+    of each phase per layer (layers after the first), the phases' algorithmic HBM
+    bytes (bf16 weights; bf16 K and V of the attended slots) and their fraction of
+    the measured HBM copy peak. With one row and the split-K MLP a layer has four
+    phases: QKV (RMSNorm, q|k|v, bias, RoPE, KV append), attention, o_proj +
+    residual, MLP (RMSNorm, gate|up, SiLU, split-K down_proj into the fixed-point
+    sums)."""
+    import numpy as np
+    dllm = importlib.import_module("distributed-llm1_b200")
+    syn = importlib.import_module("distributed-llm1_b200.synthetic")
+    cfg = dllm.PRESETS[args.model].with_(kv_dtype="bf16", max_pos=args.kv_len + 64 + tokens + 8)
+    if args.layers:
+        cfg = cfg.with_(num_layers=args.layers)
+    ctx = dllm.initKernels(0, cfg)
+    ld = dllm.LeaderPipeline(ctx, (0, cfg.num_layers))
+    bufs = syn.device_weights(ctx, ld.stage, cfg, 0, cfg.num_layers, True, True, 0)
+    ld.stage.fill_kv_random(0, args.kv_len, seed=1)
+    ctx.synchronize(120000)
+    ld.decode_enqueue(1234, 8)
+    toks = ld.read_tokens(8)
+    cap = 8 * cfg.num_layers + 16
+    ld.stage.set_trace(cap)
+    runs = []
+    for _ in range(tokens):
+        ld.decode_enqueue(toks[-1], 1)
+        toks = ld.read_tokens(1)
+        t = ld.stage.read_trace(cap).astype(np.int64)
+        runs.append(np.diff(t[:int(np.count_nonzero(t))]) / 1000.0)
+    d = np.median(np.stack(runs), axis=0)
+    L, k = cfg.num_layers, len(PHASES)
+    assert len(d) >= 1 + k * L, f"unexpected trace length {len(d)} for {L} layers"
+    per_layer = d[1:1 + k * L].reshape(L, k)
+    body = per_layer[1:] if L > 1 else per_layer
+    D, I, QD, KD = cfg.hidden_size, cfg.intermediate_size, cfg.num_q_heads * cfg.head_dim, \
+        cfg.num_kv_heads * cfg.head_dim
+    T = args.kv_len + 8 + (tokens + 1) / 2
+    nbytes = {"qkv": 2 * D * (QD + 2 * KD), "attention": 2 * 2 * KD * T, "o_proj": 2 * QD * D,
+              "mlp": 2 * 3 * D * I}
+    peak, peak_kind = measured_peaks()
+    phases = {}
+    for i, name in enumerate(PHASES):
+        us = float(np.mean(body[:, i]))
+        phases[name] = {"us": us, "bytes": nbytes[name], "gbs": nbytes[name] / us / 1e3,
+                        "hbm_frac": nbytes[name] / us / 1e3 / peak}
+    tail = [float(x) for x in d[1 + k * L:]]
+    res = {"phase_trace": args.model, "kv_len": args.kv_len, "layers": L, "tokens": tokens,
+           "token_us": float(np.median([r.sum() for r in runs])), "layer_us": float(np.mean(body.sum(1))),
+           "phases": phases, "tail_us": tail, "tail": "fold of the last layer's sums, then final norm + LM head + argmax",
+           "peak_gbs": peak, "peak_kind": peak_kind}
+    del bufs
+    ld.close()
+    ctx.close()
+    return res
+
+
 def main():
     args = parse_args()
     if args.kernel_sweep:
         run_kernel_sweep(args)
+        return
+    if args.phase_trace:
+        print(json.dumps(run_phase_trace(args)), flush=True)
         return
     if args.impl == "reference":
         res = run_reference(args)
