@@ -54,6 +54,8 @@ def parse_args():
     p.add_argument("--kv-len", type=int, default=KV_LEN)
     p.add_argument("--micro", type=int, default=1,
                    help="sequences per micro-batch (N>1), or sequences decoded together (N=1)")
+    p.add_argument("--n-micro", type=int, default=0,
+                   help="N>1: micro-batches in flight (default: one per stage)")
     p.add_argument("--tc-rows", type=int, default=None,
                    help="passes of at least this many rows use the tensor-core pass (0: never; default: the library's)")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -279,8 +281,8 @@ def workload_config(args, cfg) -> dict:
         return {"workload": f"PROFILING CASE, not the benchmark: {args.model} dims, first {args.layers} layers + "
                             f"LM head, {args.kv_len}-slot synthetic bf16 KV, batch 1", "layers": args.layers}
     return {"workload": f"{args.model} greedy decode, {args.kv_len}-slot synthetic bf16 KV per sequence, "
-                        f"{'batch 1 on one GPU' if args.gpus == 1 else f'{args.gpus}-stage pipeline, {args.gpus} micro-batches of {args.micro}'}",
-            "batch": 1 if args.gpus == 1 else args.gpus * args.micro, "kv_len": args.kv_len,
+                        f"{'batch 1 on one GPU' if args.gpus == 1 else f'{args.gpus}-stage pipeline, {args.n_micro or args.gpus} micro-batches of {args.micro}'}",
+            "batch": 1 if args.gpus == 1 else (args.n_micro or args.gpus) * args.micro, "kv_len": args.kv_len,
             "parallelism": f"pp{args.gpus}", "kv_dtype": getattr(cfg, "kv_dtype", "bf16"), "weights": "bf16",
             "l2_policy": "inputs larger than L2 (weights 15 GB per token)"}
 

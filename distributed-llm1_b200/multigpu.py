@@ -228,7 +228,7 @@ def bench_pipeline(args, bench):
     dllm = importlib.import_module("distributed-llm1_b200")
     rank, world, local = init_distributed("nccl")
     assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE {world}"
-    B, m = world, args.micro
+    B, m = (args.n_micro or world), args.micro
     e2e_steps = max(2, args.steps // 2)
     steps_total = args.warmup + args.steps + e2e_steps + 4
     cfg = dllm.PRESETS[args.model].with_(kv_dtype="bf16", max_seqs=B * m,
